@@ -1,0 +1,466 @@
+"""Decode-step benchmark of the paged KV-cache path on B200.
+
+Workload (one "step"): one decode token for every sequence of the batch,
+through all 32 layers: fused RoPE + slot-mapped append of the token's K/V
+(and RoPE of q), then paged split-K GQA attention over the sequence's
+blocks.  Shape: Llama-3-8B attention (32 query heads, 8 KV heads, head_dim
+128), block_size 16, 64 sequences per GPU with context lengths uniform in
+[128, 4096] (seed 1), blocks drawn from a randomly permuted pool sized at
+1.25x need.  fp32 K/V storage is the headline (the reference's type); the
+bf16-storage variant is measured in the same run.  Synthetic data (numpy /
+torch seeded normal), no dataset.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU: one process per GPU (torchrun); sequences are sharded across
+GPUs by balanced context sum, each GPU runs its own pool, no collective on
+the data path ("weak" scaling: 64 sequences per GPU).  Rank 0 prints one
+JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "s1-infer_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "paged decode-attn KV GB/s/GPU (% HBM peak); decode tok/s at 1/2/4/8 B200"
+LAYERS, HQ, HKV, D, BS = 32, 32, 8, 128, 16
+SEQS_PER_GPU = 64
+CTX_LO, CTX_HI, CTX_SEED = 128, 4096, 1
+WORKLOAD = "cfg2: batched ragged paged decode, Llama-3-8B attention shape"
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def contexts(n_gpus):
+    """Global batch of 64*N context lengths, split across ranks by greedy
+    balanced context sum (64 sequences per rank)."""
+    rng = np.random.default_rng(CTX_SEED)
+    ctx = rng.integers(CTX_LO, CTX_HI + 1, size=SEQS_PER_GPU * n_gpus)
+    order = np.argsort(-ctx, kind="stable")
+    loads = np.zeros(n_gpus)
+    counts = np.zeros(n_gpus, int)
+    share = [[] for _ in range(n_gpus)]
+    for i in order:
+        cand = [r for r in range(n_gpus) if counts[r] < SEQS_PER_GPU]
+        r = min(cand, key=lambda x: loads[x])
+        share[r].append(int(ctx[i]))
+        loads[r] += ctx[i]
+        counts[r] += 1
+    return share
+
+
+def decode_bytes(ctx_after, elem):
+    """Algorithmic bytes of one decode-attention launch (one layer): K and V
+    of every context token once per KV head, q in and out (fp32), and the
+    block-table entries."""
+    c = np.asarray(ctx_after, np.int64)
+    return int((c * 2 * HKV * D * elem).sum() + len(c) * HQ * D * (4 + 4) + ((c + BS - 1) // BS * 4).sum())
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons of this rank's GPU, sampled every
+    200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        import torch
+        self.proc = None
+        self.lines = []
+        gid = None
+        try:
+            pr = torch.cuda.get_device_properties(device)
+            gid = "%08X:%02X:%02X.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+        except Exception:
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            gid = vis.split(",")[device] if vis else str(device)
+        self.gid = gid
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gid}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- ours ---
+
+def run_variant(s1kv, torch, dtype, ctx, steps, warmup, rank, world, timed_e2e, sample_clocks):
+    elem = 4 if dtype == "f32" else 2
+    B = len(ctx)
+    total_steps = 2 * (steps + warmup) + 2
+    need = sum((c + total_steps + BS - 1) // BS for c in ctx)
+    max_blocks = int(need * 1.25)
+    rng = np.random.default_rng(1000 + rank)
+    order = rng.permutation(max_blocks).astype(np.int32)
+    pool = s1kv.Pool(LAYERS, HKV, D, max_blocks, BS, dtype=dtype, initial_free_list=order, max_seqs=max(256, B))
+    seqs = list(range(B))
+    gen = torch.Generator(device="cuda").manual_seed(17 + rank)
+    # prefill: random post-RoPE K/V for every context token, layer by layer
+    with pool.batch(seqs, ctx, [0] * B) as b:
+        for layer in range(LAYERS):
+            k = torch.randn((sum(ctx), HKV, D), device="cuda", generator=gen)
+            v = torch.randn((sum(ctx), HKV, D), device="cuda", generator=gen)
+            b.rope_append(layer, k, v)
+            del k, v
+    torch.cuda.synchronize()
+    q = torch.randn((LAYERS, B, HQ, D), device="cuda", generator=gen)
+    kn = torch.randn((LAYERS, B, HKV, D), device="cuda", generator=gen)
+    vn = torch.randn((LAYERS, B, HKV, D), device="cuda", generator=gen)
+    q_rot = torch.empty((LAYERS, B, HQ, D), device="cuda")
+    out = torch.empty((LAYERS, B, HQ, D), device="cuda")
+
+    def step(ev=None):
+        with pool.batch(seqs, [1] * B) as bt:
+            for layer in range(LAYERS):
+                bt.rope_append(layer, kn[layer], vn[layer], q=q[layer], q_out=q_rot[layer])
+                if ev is not None:
+                    ev[layer][0].record()
+                bt.attention(layer, q_rot[layer], out=out[layer])
+                if ev is not None:
+                    ev[layer][1].record()
+
+    for _ in range(warmup):
+        step()
+    barrier(torch, world)
+    torch.cuda.synchronize()
+    ctx_before = [pool.length(s) for s in seqs]
+    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(LAYERS)]
+           for _ in range(steps)]
+    clocks = ClockSampler(torch.cuda.current_device()) if sample_clocks else None
+    if clocks:
+        clocks.start()
+    launches0 = s1kv.launch_count()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(steps):
+        step(evs[i])
+    t1.record()
+    torch.cuda.synchronize()
+    launches = s1kv.launch_count() - launches0
+    clk = clocks.stop() if clocks else None
+    elapsed_ms = t0.elapsed_time(t1)
+    attn_ms = [evs[i][layer][0].elapsed_time(evs[i][layer][1]) for i in range(steps) for layer in range(LAYERS)]
+    attn_bytes = sum(decode_bytes([c + i + 1 for c in ctx_before], elem) for i in range(steps)) * LAYERS
+    res = {
+        "elapsed_ms": elapsed_ms,
+        "attn_ms_total": float(sum(attn_ms)),
+        "attn_launches": len(attn_ms),
+        "attn_bytes": attn_bytes,
+        "bytes_per_launch": attn_bytes / len(attn_ms),
+        "avg_launch_ms": float(np.mean(attn_ms)),
+        "launches": launches,
+        "clocks": clk,
+        "tokens": B * steps,
+        "kv_bytes_step": attn_bytes / steps,
+    }
+    if timed_e2e:
+        hq = torch.empty((LAYERS, B, HQ, D), pin_memory=True)
+        hk = torch.empty((LAYERS, B, HKV, D), pin_memory=True)
+        hv = torch.empty((LAYERS, B, HKV, D), pin_memory=True)
+        ho = torch.empty((LAYERS, B, HQ, D), pin_memory=True)
+        hq.copy_(q)
+        hk.copy_(kn)
+        hv.copy_(vn)
+
+        def step_host():
+            with pool.batch(seqs, [1] * B) as bt:
+                for layer in range(LAYERS):
+                    bt.layer_host(layer, hq[layer], hk[layer], hv[layer], ho[layer], HQ)
+
+        for _ in range(warmup):
+            step_host()
+        barrier(torch, world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step_host()
+        e1.record()
+        torch.cuda.synchronize()
+        res["e2e_ms"] = e0.elapsed_time(e1)
+        res["h2d_bytes_per_step"] = LAYERS * (hq[0].numel() + hk[0].numel() + hv[0].numel()) * 4
+        res["d2h_bytes_per_step"] = LAYERS * ho[0].numel() * 4
+    assert pool.check_device() == 0
+    pool.close()
+    del q, kn, vn, q_rot, out
+    torch.cuda.empty_cache()
+    return res
+
+
+def barrier(torch, world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(torch, world, x):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(torch, world, x):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def cpu_reference_sample(ctx, n_threads, layers_sampled=1, repeats=2, seed=5):
+    """Times the reference's GQA_attention_paged (oracle/_ref, compiled from
+    the reference sources) on one decode step of `ctx` sequences over
+    `layers_sampled` layer pools, fanned over (layer, sequence) tasks with
+    the reference's ThreadPool.  Falls back to the C restatement
+    (oracle/kvoracle.c, one thread) when the reference library is absent."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    B = len(ctx)
+    need = sum((c + 1 + BS - 1) // BS for c in ctx) + 4
+    kind = "reference" if O.ref_available() else "port"
+    q = rng.standard_normal((layers_sampled, B, HQ, D), dtype=np.float32)
+    if kind == "reference":
+        pools = [O.RefPool(HKV, D, need, BS) for _ in range(layers_sampled)]
+    else:
+        pools = [O.Pool(HKV, D, need, BS) for _ in range(layers_sampled)]
+        n_threads = 1
+    for p in pools:
+        for s, c in enumerate(ctx):
+            k = rng.standard_normal((c + 1, HKV, D), dtype=np.float32)
+            p.append(s, k, k)
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        if kind == "reference":
+            O.ref_decode_batch(pools, np.arange(B), q, HQ, HKV, D, n_threads)
+        else:
+            for li, p in enumerate(pools):
+                for s in range(B):
+                    p.attention(s, q[li, s:s + 1], HQ)
+        times.append(time.perf_counter() - t0)
+    t_layer = min(times) / layers_sampled
+    tok_s = B / (LAYERS * t_layer)
+    kv_bytes = decode_bytes([c + 1 for c in ctx], 4)
+    return {
+        "value": tok_s,
+        "unit": "tok/s",
+        "cores": n_threads,
+        "kind": kind,
+        "sample": f"{layers_sampled} of {LAYERS} layers x {B} sequences x 1 decode step (fp32), "
+                  f"best of {repeats}; per-layer time scaled x{LAYERS}",
+        "kv_gbs": kv_bytes / t_layer / 1e9,
+        "layer_s": t_layer,
+    }
+
+
+def run_ours(args):
+    import torch
+    import s1kv
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    share = contexts(world)[rank]
+    peak, peak_kind = load_peaks()
+    res = {}
+    for dtype in ("f32", "bf16"):
+        res[dtype] = run_variant(s1kv, torch, dtype, share, args.steps, args.warmup, rank, world,
+                                 timed_e2e=True, sample_clocks=(dtype == "f32"))
+    h = res["f32"]
+    elapsed = max_over_ranks(torch, world, h["elapsed_ms"])
+    tokens = sum_over_ranks(torch, world, h["tokens"])
+    e2e_ms = max_over_ranks(torch, world, h["e2e_ms"])
+    bf = res["bf16"]
+    bf_elapsed = max_over_ranks(torch, world, bf["elapsed_ms"])
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_reference_sample(share, os.cpu_count() or 1)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    achieved = h["bytes_per_launch"] / (h["avg_launch_ms"] * 1e-3) / 1e9
+    bf_achieved = bf["bytes_per_launch"] / (bf["avg_launch_ms"] * 1e-3) / 1e9
+    line = {
+        "metric": METRIC,
+        "value": tokens / (elapsed * 1e-3),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded normal Q/K/V, seeded context lengths and block permutation)",
+        "config": {"workload": WORKLOAD, "layers": LAYERS, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+                   "block_size": BS, "seqs_per_gpu": SEQS_PER_GPU, "global_batch": SEQS_PER_GPU * world,
+                   "ctx": f"U[{CTX_LO},{CTX_HI}] seed {CTX_SEED}", "pool": "1.25x need, permuted",
+                   "kv_storage": "fp32", "parallelism": f"sequence-sharded x{world}, no collective",
+                   "l2": "inputs larger than L2 (1.1 GB of K/V per layer-step)"},
+        "kv_gbs_per_gpu": h["kv_bytes_step"] / (h["elapsed_ms"] / args.steps * 1e-3) / 1e9,
+        "hbm_frac_step": h["kv_bytes_step"] / (h["elapsed_ms"] / args.steps * 1e-3) / 1e9 / peak,
+        "roofline": {"bound": "hbm", "kernel": "paged split-K decode attention (decode + combine)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
+                     else "fallback 6650 GB/s", "bytes_per_launch": h["bytes_per_launch"],
+                     "avg_launch_ms": h["avg_launch_ms"], "traffic": None},
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h["h2d_bytes_per_step"],
+                "d2h_bytes_per_step": h["d2h_bytes_per_step"],
+                "path": "s1kv_batch_layer_host (C ABI, pinned host buffers, copies in the timed region)"},
+        "gpu_launches": h["launches"],
+        "clocks": h["clocks"],
+        "variants": {"bf16_kv": {
+            "value": sum_over_ranks(torch, 1, bf["tokens"]) * world / (bf_elapsed * 1e-3), "unit": "tok/s",
+            "ms_per_step": bf_elapsed / args.steps,
+            "kv_gbs_per_gpu": bf["kv_bytes_step"] / (bf["elapsed_ms"] / args.steps * 1e-3) / 1e9,
+            "roofline": {"achieved": bf_achieved, "peak": peak, "frac": bf_achieved / peak,
+                         "avg_launch_ms": bf["avg_launch_ms"], "bytes_per_launch": bf["bytes_per_launch"]},
+            "e2e_tok_s": bf["tokens"] * world / (bf["e2e_ms"] * 1e-3)}},
+        "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+    }
+    print(json.dumps(line))
+
+
+# ------------------------------------------------------------ reference ---
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    if rank != 0:
+        return
+    share = contexts(world)[0]
+    from oracle import oracle as O
+    n_threads = os.cpu_count() or 1
+    rng = np.random.default_rng(5)
+    B = len(share)
+    need = sum((c + 1 + BS - 1) // BS for c in share) + 4
+    kind = "reference" if O.ref_available() else "port"
+    pool = O.RefPool(HKV, D, need, BS) if kind == "reference" else O.Pool(HKV, D, need, BS)
+    for s, c in enumerate(share):
+        k = rng.standard_normal((c + 1, HKV, D), dtype=np.float32)
+        pool.append(s, k, k)
+    q = rng.standard_normal((1, B, HQ, D), dtype=np.float32)
+
+    def one_layer():
+        if kind == "reference":
+            O.ref_decode_batch([pool], np.arange(B), q, HQ, HKV, D, n_threads)
+        else:
+            for s in range(B):
+                pool.attention(s, q[0, s:s + 1], HQ)
+
+    for _ in range(args.warmup):
+        one_layer()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one_layer()
+    dt = (time.perf_counter() - t0) / args.steps
+    tok_s = B / (LAYERS * dt)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * LAYERS * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded normal Q/K/V, seeded context lengths)",
+        "config": {"workload": WORKLOAD, "layers": LAYERS, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+                   "block_size": BS, "seqs_per_gpu": SEQS_PER_GPU, "global_batch": SEQS_PER_GPU * world,
+                   "ctx": f"U[{CTX_LO},{CTX_HI}] seed {CTX_SEED}", "kv_storage": "fp32",
+                   "parallelism": "host CPU, rank 0 only"},
+        "kv_gbs_per_gpu": decode_bytes([c + 1 for c in share], 4) / dt / 1e9,
+        "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": n_threads if kind == "reference" else 1,
+                         "kind": kind,
+                         "sample": f"each step = 1 of {LAYERS} layers x {B} sequences x 1 decode token "
+                                   f"(GQA_attention_paged over the reference ThreadPool); scaled x{LAYERS}"},
+        "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,270 @@
+/*
+ * s1kv.h -- C ABI of the B200 paged KV-cache engine (libs1kv.so).
+ *
+ * The engine replaces the KV-cache hot path of liamma06/s1-infer:
+ *   KVBlockPool            include/infer/kv_block_pool.h:13-45
+ *   KVView                 include/infer/kv_block_pool.h:6-11
+ *   apply_rope             include/nn/RoPE.h:4
+ *   GQA_attention(_paged)  include/nn/attention.h:8-10
+ * Reference paths above are relative to the s1-infer project root.
+ *
+ * Conventions
+ *   - Every call returns an int status (S1KV_OK on success).  The message of
+ *     the last failure on the calling thread is s1kv_last_error().
+ *   - Host bookkeeping (free list, block tables, refcounts, prefix cache) is
+ *     single-threaded per pool: drive one pool from one host thread.
+ *   - Kernel calls are asynchronous and stream-ordered on the caller's CUDA
+ *     stream (passed as void*, NULL = legacy default stream).  Device
+ *     pointers passed in are borrowed until the stream work completes.
+ *   - Unless a call says otherwise, data pointers are DEVICE pointers.
+ *   - A pool holds num_layers layers that share one block table per
+ *     sequence.  The reference keeps one KVBlockPool per layer and drives
+ *     every layer with the same append/truncate/remove sequence
+ *     (src/model/model.cpp:144-162, :297-298), so its per-layer tables are
+ *     identical; a pool with num_layers = 1 is exactly one KVBlockPool.
+ *   - Pool storage per layer is [max_blocks * block_size][num_kv_heads]
+ *     [head_dim] in the pool dtype, the reference layout
+ *     (src/infer/kv_block_pool.cpp:12-13); token i of a sequence lives at
+ *     slot table[i / block_size] * block_size + i % block_size.
+ */
+#ifndef S1KV_H
+#define S1KV_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define S1KV_OK 0
+#define S1KV_ENOBLOCKS 1 /* free list (and LRU) exhausted; ref throws runtime_error (kv_block_pool.cpp:36-38) */
+#define S1KV_ENOSEQ 2    /* unknown sequence id; ref throws runtime_error (kv_block_pool.cpp:70,151,166,195) */
+#define S1KV_EINVAL 3    /* bad argument or shape */
+#define S1KV_ECUDA 4     /* a CUDA runtime call failed */
+#define S1KV_ETIMEOUT 5  /* a bounded device-side wait ran out */
+#define S1KV_ENOMEM 6    /* device or host allocation failed */
+#define S1KV_EDEVICE 7   /* a kernel's bounds check recorded a bad slot/block */
+
+/* ---- storage dtypes ---- */
+#define S1KV_DTYPE_F32 0  /* the reference's storage type (include/core/tensor.h:5) */
+#define S1KV_DTYPE_BF16 1 /* round-to-nearest-even narrowed on append; widened like
+                             bf16_to_float (include/io/safetensors.h:156-161) */
+
+/* ---- pool flags ---- */
+#define S1KV_POOL_HOST_ONLY 1 /* bookkeeping only: no device memory; kernel calls fail */
+
+/* ---- which tensor ---- */
+#define S1KV_K 0
+#define S1KV_V 1
+
+typedef struct s1kv_pool s1kv_pool;
+typedef struct s1kv_batch s1kv_batch;
+
+typedef struct s1kv_pool_desc {
+    int32_t num_layers;   /* layers sharing one block table (>= 1) */
+    int32_t num_kv_heads; /* KVBlockPool num_heads (kv_block_pool.h:32) */
+    int32_t head_dim;     /* KVBlockPool head_dim */
+    int32_t block_size;   /* KVBlockPool block_size (default 16) */
+    int64_t max_blocks;   /* KVBlockPool max_blocks: physical blocks per layer */
+    int32_t dtype;        /* S1KV_DTYPE_* */
+    int32_t max_seqs;     /* rows of the device block table (0 = 1024) */
+    int64_t max_seq_len;  /* tokens per sequence the device table can map (0 = max_blocks * block_size) */
+    float rope_theta;     /* RoPE base; 0 = 1e6 (src/nn/RoPE.cpp:22) */
+    int32_t flags;        /* S1KV_POOL_* */
+    /* Optional initial free list, bottom .. top (the top is allocated
+     * first).  NULL = 0 .. max_blocks-1 pushed in order, so the first
+     * allocation returns max_blocks-1 (kv_block_pool.cpp:15-17).  Must be a
+     * permutation of 0 .. max_blocks-1. */
+    const int32_t* initial_free_list;
+} s1kv_pool_desc;
+
+/* Per-pool counters, for the tests and the bench. */
+typedef struct s1kv_pool_stats {
+    int64_t num_free;        /* blocks on the free list */
+    int64_t num_lru;         /* zero-refcount cached blocks (evictable) */
+    int64_t num_cached;      /* blocks registered in the prefix cache */
+    int64_t num_seqs;        /* live sequences */
+    int64_t cow_copies;      /* copy-on-write block copies queued so far */
+    int64_t evictions;       /* LRU evictions so far */
+    int64_t device_bytes;    /* device memory held by the pool */
+} s1kv_pool_stats;
+
+/* ======================== errors ======================== */
+
+const char* s1kv_last_error(void);
+const char* s1kv_status_str(int status);
+
+/* ======================== lifecycle ======================== */
+
+/* KVBlockPool::KVBlockPool (kv_block_pool.cpp:6-18).  Allocates and
+ * zero-fills K/V storage for every layer on `device`. */
+int s1kv_pool_create(const s1kv_pool_desc* desc, int device, s1kv_pool** out);
+int s1kv_pool_destroy(s1kv_pool* pool);
+int s1kv_pool_get_desc(const s1kv_pool* pool, s1kv_pool_desc* out);
+int s1kv_pool_stats_get(const s1kv_pool* pool, s1kv_pool_stats* out);
+
+/* Device base pointers of one layer's K and V storage (the KVView::base of
+ * get_k_view/get_v_view, kv_block_pool.cpp:192-223). */
+int s1kv_pool_storage(const s1kv_pool* pool, int32_t layer, void** k_base, void** v_base);
+
+/* Synchronous copy of the raw bytes of storage slots [slot0, slot0 +
+ * n_slots) of one layer's K (which = S1KV_K) or V into host memory
+ * (n_slots * num_kv_heads * head_dim elements of the pool dtype). */
+int s1kv_pool_read(s1kv_pool* pool, int32_t layer, int32_t which, int64_t slot0, int64_t n_slots, void* host_out);
+
+/* Reads and clears the device error word (synchronises the device).  Bit 0:
+ * a kernel saw a slot or block id out of range; bit 1: a bounded wait timed
+ * out.  Returns S1KV_EDEVICE / S1KV_ETIMEOUT when a bit was set. */
+int s1kv_pool_check(s1kv_pool* pool, int32_t* flags_out);
+
+/* ======================== sequence bookkeeping (host) ======================== */
+
+/* Allocation half of KVBlockPool::append (kv_block_pool.cpp:20-65): places
+ * n_tokens new tokens at the end of `seq` (created if absent, like
+ * sequences_[id]) and writes their slots to slots_out (host, may be NULL).
+ * On exhaustion returns S1KV_ENOBLOCKS with the tokens placed so far kept
+ * (*n_done), as the reference throws after partial progress.  If the last
+ * block is partially filled and shared (refcount > 1) or held by the prefix
+ * cache, it is first replaced by a private copy (copy-on-write); the copy is
+ * queued and runs on the device at the next kernel call or s1kv_flush. */
+int s1kv_seq_reserve(s1kv_pool* pool, uint64_t seq, int64_t n_tokens, int32_t* slots_out, int64_t* n_done);
+
+/* KVBlockPool::length (kv_block_pool.cpp:134-146); 0 for an unknown id. */
+int64_t s1kv_seq_length(const s1kv_pool* pool, uint64_t seq);
+int s1kv_seq_exists(const s1kv_pool* pool, uint64_t seq);
+
+/* KVBlockPool::remove (kv_block_pool.cpp:148-161).  Blocks are released in
+ * table order; a block returns to the free list when its refcount hits 0
+ * (to the LRU instead if the prefix cache holds it). */
+int s1kv_seq_remove(s1kv_pool* pool, uint64_t seq);
+
+/* KVBlockPool::truncate (kv_block_pool.cpp:163-190).  No-op when
+ * keep >= length; tail blocks are released last-first. */
+int s1kv_seq_truncate(s1kv_pool* pool, uint64_t seq, int64_t keep);
+
+/* Block sharing (no reference counterpart): dst (must not exist) starts as
+ * the first n_tokens of src, sharing its blocks with refcount + 1.  A shared
+ * partial tail is copied on the first append by either side. */
+int s1kv_seq_fork(s1kv_pool* pool, uint64_t src, uint64_t dst, int64_t n_tokens);
+
+/* Physical block ids of `seq` (the KVView::block_table).  *n_out = table
+ * length even when cap is smaller. */
+int s1kv_block_table(const s1kv_pool* pool, uint64_t seq, int32_t* out, int64_t cap, int64_t* n_out);
+int s1kv_block_refcount(const s1kv_pool* pool, int32_t block, int32_t* rc_out);
+/* Free list bottom .. top and the LRU list oldest .. newest (host arrays). */
+int s1kv_free_list(const s1kv_pool* pool, int32_t* out, int64_t cap, int64_t* n_out);
+int s1kv_lru_list(const s1kv_pool* pool, int32_t* out, int64_t cap, int64_t* n_out);
+
+/* ======================== prefix cache (host) ======================== */
+/* Replaces the reference's single-sequence disk prefix and its truncate
+ * rewind (src/demo.cpp:10-41, src/model/model.cpp:239-240). */
+
+/* Registers the full blocks of `seq` covering tokens[0:n_tokens) (host
+ * int32 token ids) under chained block hashes.  *n_added = blocks newly
+ * registered. */
+int s1kv_prefix_insert(s1kv_pool* pool, uint64_t seq, const int32_t* tokens, int64_t n_tokens, int64_t* n_added);
+
+/* Creates `dst` from the longest registered chain matching tokens[0:n):
+ * matching blocks gain a reference (leaving the LRU).  *n_hit = tokens
+ * covered, a multiple of block_size. */
+int s1kv_prefix_match(s1kv_pool* pool, uint64_t dst, const int32_t* tokens, int64_t n_tokens, int64_t* n_hit);
+
+/* Chained hash of one block of ids (for host-side tooling and tests). */
+uint64_t s1kv_block_hash(uint64_t parent, const int32_t* tokens, int64_t n);
+
+/* save_prefix_cache (src/demo.cpp:33-41): for every layer in order, writes
+ * seq's K then V as raw fp32 [length][num_kv_heads][head_dim]. */
+int s1kv_prefix_save(s1kv_pool* pool, uint64_t seq, const char* path);
+/* load_prefix_cache (src/demo.cpp:10-31): reads n_tokens tokens of that
+ * layout and appends them to seq in every layer.  S1KV_EINVAL if the file
+ * is missing or short (the reference returns false). */
+int s1kv_prefix_load(s1kv_pool* pool, uint64_t seq, int64_t n_tokens, const char* path);
+
+/* ======================== kernels (device, async) ======================== */
+
+/* Runs queued copy-on-write block copies and device block-table updates. */
+int s1kv_flush(s1kv_pool* pool, void* stream);
+
+/* Data half of KVBlockPool::append: k, v [n][num_kv_heads][head_dim] fp32
+ * are stored at slots[n] (device int32) of `layer`, narrowed to the pool
+ * dtype (kv_block_pool.cpp:53-59). */
+int s1kv_append(s1kv_pool* pool, int32_t layer, const float* k, const float* v, const int32_t* slots, int64_t n,
+                void* stream);
+
+/* Fused RoPE + append.  k is rotated at pos[t] (apply_rope, RoPE.cpp:6-39)
+ * and stored with v at slots[t].  When q_in is non-NULL, q_in [n][n_q_heads]
+ * [head_dim] is rotated at the same positions into q_out. */
+int s1kv_rope_append(s1kv_pool* pool, int32_t layer, const float* q_in, float* q_out, int32_t n_q_heads,
+                     const float* k, const float* v, const int32_t* slots, const int32_t* pos, int64_t n,
+                     void* stream);
+
+/* apply_rope(input, start_pos) (RoPE.cpp:6-39) of x [n][n_heads][head_dim]
+ * on the current CUDA device: token t rotates at start_pos + t.  theta 0 =
+ * 1e6.  x and out may alias. */
+int s1kv_apply_rope(const float* x, float* out, int64_t start_pos, int64_t n, int32_t n_heads, int32_t head_dim,
+                    float theta, void* stream);
+
+/* KVBlockPool::get_k / get_v (kv_block_pool.cpp:67-132): gathers `seq`'s
+ * tokens of one layer into out [length][num_kv_heads][head_dim] fp32. */
+int s1kv_gather(s1kv_pool* pool, int32_t layer, uint64_t seq, int32_t which, float* out, void* stream);
+
+/* Copies whole blocks src[i] -> dst[i] (device int32 ids) in every layer,
+ * K and V: the copy-on-write kernel. */
+int s1kv_cow_copy(s1kv_pool* pool, const int32_t* src, const int32_t* dst, int64_t n, void* stream);
+
+/* GQA_attention_paged (attention.cpp:128-239) for sequences of one layer.
+ * q [sum q_lens][n_q_heads][head_dim] fp32 holds each sequence's q_len
+ * query rows back to back; row i of a sequence of length L attends to
+ * tokens 0 .. (L - q_len) + i.  out has q's shape.  seqs / q_lens are host
+ * arrays. */
+int s1kv_attention(s1kv_pool* pool, int32_t layer, const uint64_t* seqs, const int32_t* q_lens, int32_t n_seqs,
+                   const float* q, float* out, int32_t n_q_heads, void* stream);
+
+/* GQA_attention (attention.cpp:13-126) over contiguous device K/V
+ * [kv_len][n_kv_heads][head_dim] fp32. */
+int s1kv_attention_contig(const float* q, const float* k, const float* v, int64_t q_len, int64_t kv_len,
+                          int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim, float* out, void* stream);
+
+/* ======================== batched step (device, async) ======================== */
+/* One decode or prefill step of many sequences, amortising the host
+ * bookkeeping over all layers: begin reserves n_append[i] slots for each
+ * sequence and uploads the step's slots, positions, block tables and work
+ * lists once; then per layer rope_append and attention run on that upload.
+ * q_len[i] = rows of attention queries for sequence i (NULL = n_append).
+ * A decode step is n_append = q_len = 1 for every sequence. */
+int s1kv_batch_begin(s1kv_pool* pool, const uint64_t* seqs, const int32_t* n_append, const int32_t* q_lens,
+                     int32_t n_seqs, void* stream, s1kv_batch** out);
+/* Total appended tokens and query rows of the batch. */
+int s1kv_batch_sizes(const s1kv_batch* batch, int64_t* n_tokens, int64_t* n_rows);
+/* RoPE + append of this step's k, v [n_tokens][num_kv_heads][head_dim]; q
+ * [n_rows][n_q_heads][head_dim] rotated into q_out when q_in is non-NULL
+ * (n_rows must equal n_tokens then). */
+int s1kv_batch_rope_append(s1kv_batch* batch, int32_t layer, const float* q_in, float* q_out, int32_t n_q_heads,
+                           const float* k, const float* v, void* stream);
+/* Append without RoPE (KVBlockPool::append data movement). */
+int s1kv_batch_append(s1kv_batch* batch, int32_t layer, const float* k, const float* v, void* stream);
+/* Paged GQA attention of the batch's query rows (post-RoPE q). */
+int s1kv_batch_attention(s1kv_batch* batch, int32_t layer, const float* q, float* out, int32_t n_q_heads,
+                         void* stream);
+/* End-to-end layer step with HOST buffers (pinned for full speed): copies
+ * q, k, v in, runs RoPE+append and attention, copies out back.  Shapes as
+ * above.  The copies are stream-ordered; synchronise before reading out. */
+int s1kv_batch_layer_host(s1kv_batch* batch, int32_t layer, const float* h_q, const float* h_k, const float* h_v,
+                          float* h_out, int32_t n_q_heads, void* stream);
+int s1kv_batch_end(s1kv_batch* batch, void* stream);
+
+/* ======================== introspection ======================== */
+
+/* Number of kernel launches this library issued on the calling process
+ * (all pools), for launch accounting. */
+int64_t s1kv_launch_count(void);
+/* Split size (tokens per work item) the last s1kv_batch_begin chose, and
+ * the number of attention work items. */
+int s1kv_batch_plan(const s1kv_batch* batch, int32_t* split_tokens, int64_t* n_items);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* S1KV_H */

@@ -1,0 +1,229 @@
+// internal.h -- shared declarations of libs1kv (host bookkeeping + kernels).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <list>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "s1kv.h"
+
+namespace s1kv {
+
+// ---------------------------------------------------------------- errors --
+int set_error(int status, const char* fmt, ...);
+int cuda_error(cudaError_t e, const char* what);
+#define S1KV_CUDA(call)                                           \
+    do {                                                          \
+        cudaError_t e_ = (call);                                  \
+        if (e_ != cudaSuccess) return ::s1kv::cuda_error(e_, #call); \
+    } while (0)
+
+extern std::atomic<int64_t> g_launches;
+
+// Device error word bits (one word per device, shared by every kernel).
+constexpr int kErrBounds = 1;
+constexpr int kErrTimeout = 2;
+int* device_error_word(int device);
+
+// -------------------------------------------------------- device structs --
+// One query row of attention: its sequence's block-table row, the number
+// of tokens it attends to (causal limit + 1), how many split-K items cover
+// it and where its partial results start.
+struct RowMeta {
+    int32_t table_row;
+    int32_t kv_len;
+    int32_t n_split;
+    int32_t part_off;
+};
+
+// One split-K work item: query row and split index.
+struct WorkItem {
+    int32_t row;
+    int32_t split;
+};
+
+struct AttnParams {
+    const float* q;        // [rows][Hq][D] fp32, post-RoPE
+    float* out;            // [rows][Hq][D] fp32
+    float* part_o;         // [n_part][Hkv][G][D]
+    float* part_ml;        // [n_part][Hkv][G][2]  (max in log2 domain, sum)
+    const int32_t* table;  // [max_seqs][max_bps], NULL = contiguous K/V
+    const RowMeta* rows;
+    const WorkItem* items;
+    const void* kbase;     // layer base of K storage (pool dtype)
+    const void* vbase;
+    int64_t num_slots;     // rows in one layer's storage (bounds)
+    int32_t max_bps;
+    int32_t max_blocks;
+    int32_t n_rows;
+    int32_t n_items;
+    int32_t split_tokens;
+    int32_t block_size;
+    int32_t Hq, Hkv, D;
+    int32_t layer;
+    float scale_log2;      // log2(e) / sqrt(D)
+    int* err;
+};
+
+struct AppendParams {
+    const float* k;        // [n][Hkv][D]
+    const float* v;
+    const float* q_in;     // [n][Hq][D] or NULL
+    float* q_out;
+    const int32_t* slots;  // [n]
+    const int32_t* pos;    // [n] (RoPE only)
+    void* kpool;           // layer base (pool dtype)
+    void* vpool;
+    const float2* rope;    // [rope_cap][D/2] (cos, sin)
+    int64_t rope_cap;
+    int64_t num_slots;
+    int64_t n;
+    int32_t Hkv, Hq, D;
+    int* err;
+};
+
+// ------------------------------------------------------------ RoPE table --
+// cos/sin of every (position, pair) computed on the host with the exact
+// float expression of src/nn/RoPE.cpp:22-24 and uploaded once; device
+// transcendental functions do not round like the host C library, and the
+// appended K bytes must match the reference bit for bit.
+const float2* rope_table(int device, int D, float theta, int64_t min_positions, int64_t* cap, cudaStream_t stream,
+                         int* status);
+
+// ------------------------------------------------------------- staging --
+// Pinned host + device buffer pairs reused round-robin for per-step
+// metadata uploads.  A segment is reused only after the event recorded at
+// its release has completed.
+struct StageSeg {
+    char* h = nullptr;
+    char* d = nullptr;
+    size_t cap = 0;
+    cudaEvent_t ev = nullptr;
+    bool pending = false;  // an event recorded at release guards reuse
+    bool in_use = false;   // held by a live batch or an in-progress flush
+};
+
+struct Stager {
+    static constexpr int kSegs = 6;
+    StageSeg seg[kSegs];
+    int next = 0;
+    int acquire(size_t bytes, StageSeg** out);
+    int release(StageSeg* s, cudaStream_t stream);
+    void destroy();
+};
+
+// Growable device buffer; growth synchronises the device first.
+struct DevBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+    int ensure(size_t bytes);
+    void destroy();
+};
+
+// ---------------------------------------------------------------- pool --
+struct Seq {
+    std::vector<int32_t> table;
+    int64_t tokens_in_last = 0;
+    int32_t row = -1;         // device block-table row
+    int64_t synced = 0;       // table entries [0, synced) mirrored on the device
+};
+
+struct CacheEntry {
+    uint64_t hash = 0;
+    uint64_t parent = 0;
+    std::vector<int32_t> tokens;
+};
+
+struct TableUpdate {
+    int32_t row, col, block;
+};
+
+}  // namespace s1kv
+
+struct s1kv_pool {
+    s1kv_pool_desc desc{};
+    int device = 0;
+    bool host_only = false;
+    // device storage
+    char* k = nullptr;
+    char* v = nullptr;
+    size_t elem = 4;
+    size_t layer_bytes = 0;   // bytes of one layer of K (or V)
+    int64_t num_slots = 0;    // max_blocks * block_size
+    int32_t* d_table = nullptr;
+    int32_t max_bps = 0;
+    int* d_err = nullptr;
+    CUtensorMap tmap_k{};
+    CUtensorMap tmap_v{};
+    bool tmap_ok = false;
+    // host bookkeeping
+    std::vector<int32_t> free_list;   // LIFO, back() allocated first
+    std::vector<int32_t> rc;
+    std::vector<int32_t> cached;      // 1 if the prefix cache holds the block
+    std::list<int32_t> lru;           // zero-refcount cached blocks, oldest first
+    std::vector<std::list<int32_t>::iterator> lru_pos;
+    std::vector<uint8_t> in_lru;
+    std::unordered_map<uint64_t, s1kv::Seq> seqs;
+    std::vector<int32_t> free_rows;
+    std::unordered_multimap<uint64_t, int32_t> cache_map;  // hash -> block
+    std::vector<s1kv::CacheEntry> cache_entry;             // per block
+    int64_t num_cached = 0;
+    int64_t max_len_seen = 0;
+    // pending device work
+    std::vector<int32_t> pend_cow_src, pend_cow_dst;
+    std::vector<uint64_t> dirty;      // sequences whose device table row is stale
+    std::vector<s1kv::TableUpdate> pend_rows_cleared;
+    // stats
+    int64_t cow_copies = 0;
+    int64_t evictions = 0;
+    // device helpers
+    s1kv::Stager stager;
+    s1kv::DevBuf scratch;             // split-K partials
+    s1kv::DevBuf io;                  // host-pointer step buffers
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t io_ev[4] = {nullptr, nullptr, nullptr, nullptr};
+};
+
+struct s1kv_batch {
+    s1kv_pool* pool = nullptr;
+    s1kv::StageSeg* seg = nullptr;
+    int64_t n_tokens = 0;     // appended tokens
+    int64_t n_rows = 0;       // attention query rows
+    int64_t n_items = 0;      // split-K work items
+    int64_t n_part = 0;       // partial-result slots
+    int32_t split_tokens = 0;
+    int64_t max_pos = 0;      // largest position appended + 1
+    bool decode_rows = true;  // every row has q_len 1 for its sequence
+    // device views into seg->d
+    const int32_t* d_slots = nullptr;
+    const int32_t* d_pos = nullptr;
+    const s1kv::RowMeta* d_rows = nullptr;
+    const s1kv::WorkItem* d_items = nullptr;
+    std::vector<s1kv::RowMeta> rows;  // host copy (for dispatch decisions)
+};
+
+namespace s1kv {
+
+// --------------------------------------------------------------- kernels --
+int launch_table_update(const TableUpdate* d_upd, int64_t n, int32_t* table, int32_t max_bps, cudaStream_t stream);
+int launch_cow(s1kv_pool* pool, const int32_t* d_src, const int32_t* d_dst, int64_t n, cudaStream_t stream);
+int launch_append(const AppendParams& p, int dtype, bool rope, cudaStream_t stream);
+int launch_rope(const float* x, float* out, const float2* table, int64_t table_cap, int64_t start_pos, int64_t n,
+                int32_t H, int32_t D, int* err, cudaStream_t stream);
+int launch_gather(s1kv_pool* pool, int32_t layer, int32_t row, int64_t len, int which, float* out,
+                  cudaStream_t stream);
+// Paged attention over a prepared work list; picks the TMA split-K decode
+// kernel when the shape allows it and the generic kernel otherwise.
+int launch_attention(s1kv_pool* pool, const AttnParams& p, int dtype, cudaStream_t stream);
+int launch_attention_generic(const AttnParams& p, int dtype, cudaStream_t stream);
+bool tma_attention_supported(int dtype, int D, int G, int block_size);
+int tma_warps_per_cta(int dtype, int D);
+int make_tensor_maps(s1kv_pool* pool);
+
+}  // namespace s1kv

@@ -1,0 +1,339 @@
+// kernels.cu -- data-movement kernels of the paged KV cache: fused RoPE +
+// slot-mapped append, plain append, standalone RoPE, copy-on-write block
+// copy, gather (materialise a sequence), device block-table updates.
+//
+// All are HBM-bound byte movers: every thread moves 16-byte vectors, grids
+// are sized in multiples of the 148 SMs, and nothing is staged through
+// shared memory because nothing is reused.
+#include <cuda_bf16.h>
+
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "internal.h"
+
+namespace s1kv {
+
+constexpr int kSMs = 148;
+
+// ------------------------------------------------------------ bf16 utils --
+// Round-to-nearest-even narrowing; NaN becomes the quiet NaN 0x7FC0 with
+// the input's sign.  Written out in integer arithmetic so the host oracle
+// and the device agree on every input.
+__device__ __forceinline__ uint16_t f32_to_bf16(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu) != 0) return (uint16_t)(((u >> 16) & 0x8000u) | 0x7FC0u);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+
+__device__ __forceinline__ void flag_error(int* err, int bit) {
+    if (err) atomicOr(err, bit);
+}
+
+// -------------------------------------------------------- table updates --
+__global__ void table_update_kernel(const TableUpdate* __restrict__ upd, int64_t n, int32_t* __restrict__ table,
+                                    int32_t max_bps) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        TableUpdate u = upd[i];
+        table[(int64_t)u.row * max_bps + u.col] = u.block;
+    }
+}
+
+int launch_table_update(const TableUpdate* d_upd, int64_t n, int32_t* table, int32_t max_bps, cudaStream_t stream) {
+    int grid = (int)std::min<int64_t>((n + 255) / 256, kSMs * 4);
+    table_update_kernel<<<grid, 256, 0, stream>>>(d_upd, n, table, max_bps);
+    g_launches++;
+    S1KV_CUDA(cudaGetLastError());
+    return S1KV_OK;
+}
+
+// ------------------------------------------------------ copy-on-write ----
+// Copies whole physical blocks src[i] -> dst[i] of K and V in every layer.
+// One block of one layer is bs * Hkv * D * elem bytes, contiguous.
+__global__ void cow_kernel(const int32_t* __restrict__ src, const int32_t* __restrict__ dst, int64_t n_pairs,
+                           int32_t n_layers, char* __restrict__ k, char* __restrict__ v, size_t layer_bytes,
+                           size_t block_bytes, int32_t max_blocks, int* err) {
+    const int64_t vec_per_block = (int64_t)(block_bytes / 16);
+    const int64_t total = n_pairs * n_layers * 2 * vec_per_block;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t e = i % vec_per_block;
+        int64_t r = i / vec_per_block;
+        int which = (int)(r & 1);
+        r >>= 1;
+        int64_t layer = r % n_layers;
+        int64_t pair = r / n_layers;
+        int32_t s = src[pair], d = dst[pair];
+        if ((uint32_t)s >= (uint32_t)max_blocks || (uint32_t)d >= (uint32_t)max_blocks) {
+            flag_error(err, kErrBounds);
+            continue;
+        }
+        char* base = (which ? v : k) + layer * layer_bytes;
+        const int4* ps = reinterpret_cast<const int4*>(base + (size_t)s * block_bytes) + e;
+        int4* pd = reinterpret_cast<int4*>(base + (size_t)d * block_bytes) + e;
+        *pd = __ldcs(ps);
+    }
+}
+
+int launch_cow(s1kv_pool* p, const int32_t* d_src, const int32_t* d_dst, int64_t n, cudaStream_t stream) {
+    if (n <= 0) return S1KV_OK;
+    size_t block_bytes = (size_t)p->desc.block_size * p->desc.num_kv_heads * p->desc.head_dim * p->elem;
+    if (block_bytes % 16)
+        return set_error(S1KV_EINVAL, "s1kv_cow_copy: block bytes (%zu) not a multiple of 16", block_bytes);
+    int64_t total = n * p->desc.num_layers * 2 * (int64_t)(block_bytes / 16);
+    int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, kSMs * 8));
+    cow_kernel<<<grid, 256, 0, stream>>>(d_src, d_dst, n, p->desc.num_layers, p->k, p->v, p->layer_bytes, block_bytes,
+                                         (int32_t)p->desc.max_blocks, p->d_err);
+    g_launches++;
+    S1KV_CUDA(cudaGetLastError());
+    return S1KV_OK;
+}
+
+// -------------------------------------------------------------- append ----
+// Work unit = 8 rotation pairs (j .. j+7 and j+D/2 .. j+D/2+7) of one
+// (token, head): two 32-byte fp32 loads, two stores of 8 elements (32 B
+// fp32, 16 B bf16).  Units cover K heads, then V heads, then Q heads.
+//
+// Rotation (src/nn/RoPE.cpp:32-33): out1 = x1*c - x2*s, out2 = x2*c + x1*s,
+// each product and sum rounded separately (no fused multiply-add), as the
+// reference's build computes them.
+
+template <typename T>
+__device__ __forceinline__ void store8(T* dst, const float* x);
+
+template <>
+__device__ __forceinline__ void store8<float>(float* dst, const float* x) {
+    reinterpret_cast<float4*>(dst)[0] = make_float4(x[0], x[1], x[2], x[3]);
+    reinterpret_cast<float4*>(dst)[1] = make_float4(x[4], x[5], x[6], x[7]);
+}
+
+template <>
+__device__ __forceinline__ void store8<uint16_t>(uint16_t* dst, const float* x) {
+    uint4 w;
+    w.x = (uint32_t)f32_to_bf16(x[0]) | ((uint32_t)f32_to_bf16(x[1]) << 16);
+    w.y = (uint32_t)f32_to_bf16(x[2]) | ((uint32_t)f32_to_bf16(x[3]) << 16);
+    w.z = (uint32_t)f32_to_bf16(x[4]) | ((uint32_t)f32_to_bf16(x[5]) << 16);
+    w.w = (uint32_t)f32_to_bf16(x[6]) | ((uint32_t)f32_to_bf16(x[7]) << 16);
+    *reinterpret_cast<uint4*>(dst) = w;
+}
+
+__device__ __forceinline__ void load8(const float* src, float* x) {
+    float4 a = __ldcs(reinterpret_cast<const float4*>(src));
+    float4 b = __ldcs(reinterpret_cast<const float4*>(src) + 1);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+__device__ __forceinline__ void rotate8(float* x1, float* x2, const float2* cs) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        float c = cs[i].x, s = cs[i].y;
+        float a = __fsub_rn(__fmul_rn(x1[i], c), __fmul_rn(x2[i], s));
+        float b = __fadd_rn(__fmul_rn(x2[i], c), __fmul_rn(x1[i], s));
+        x1[i] = a;
+        x2[i] = b;
+    }
+}
+
+template <typename T, bool ROPE>
+__global__ void __launch_bounds__(256) append_vec_kernel(const AppendParams p) {
+    const int D = p.D, half = D / 2;
+    const int upr = half / 8;  // units per (token, head)
+    const int64_t kv_units = p.n * p.Hkv * upr;
+    const int64_t q_units = (ROPE && p.q_in) ? p.n * p.Hq * upr : 0;
+    const int64_t total = 2 * kv_units + q_units;
+    for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
+        int part;  // 0 = K, 1 = V, 2 = Q
+        int64_t w;
+        if (u < kv_units) { part = 0; w = u; }
+        else if (u < 2 * kv_units) { part = 1; w = u - kv_units; }
+        else { part = 2; w = u - 2 * kv_units; }
+        const int H = part == 2 ? p.Hq : p.Hkv;
+        const int j = (int)(w % upr) * 8;
+        const int64_t th = w / upr;  // token * H + head
+        const int64_t t = th / H;
+        const float* src = (part == 0 ? p.k : part == 1 ? p.v : p.q_in) + th * D;
+        float x1[8], x2[8];
+        load8(src + j, x1);
+        load8(src + half + j, x2);
+        if (ROPE && part != 1) {
+            int32_t pos = p.pos[t];
+            if ((uint64_t)pos >= (uint64_t)p.rope_cap) {
+                flag_error(p.err, kErrBounds);
+                continue;
+            }
+            float2 cs[8];
+            const float4* row = reinterpret_cast<const float4*>(p.rope + (int64_t)pos * half + j);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                float4 c = __ldg(row + i);
+                cs[2 * i] = make_float2(c.x, c.y);
+                cs[2 * i + 1] = make_float2(c.z, c.w);
+            }
+            rotate8(x1, x2, cs);
+        }
+        if (part == 2) {
+            float* dst = p.q_out + th * D;
+            store8<float>(dst + j, x1);
+            store8<float>(dst + half + j, x2);
+            continue;
+        }
+        int32_t slot = p.slots[t];
+        if ((uint64_t)slot >= (uint64_t)p.num_slots) {
+            flag_error(p.err, kErrBounds);
+            continue;
+        }
+        T* dst = reinterpret_cast<T*>(part == 0 ? p.kpool : p.vpool) + ((int64_t)slot * p.Hkv + (th % H)) * D;
+        store8<T>(dst + j, x1);
+        store8<T>(dst + half + j, x2);
+    }
+}
+
+// Element-wise fallback for head dims that are not a multiple of 16 or
+// unaligned inputs (the reference's own tests use head_dim 1 and 2).
+template <typename T, bool ROPE>
+__global__ void append_scalar_kernel(const AppendParams p) {
+    const int D = p.D, half = D / 2;
+    const int64_t kv_elems = p.n * p.Hkv * D;
+    const int64_t q_elems = (ROPE && p.q_in) ? p.n * p.Hq * D : 0;
+    const int64_t total = 2 * kv_elems + q_elems;
+    for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
+        int part;
+        int64_t w;
+        if (u < kv_elems) { part = 0; w = u; }
+        else if (u < 2 * kv_elems) { part = 1; w = u - kv_elems; }
+        else { part = 2; w = u - 2 * kv_elems; }
+        const int H = part == 2 ? p.Hq : p.Hkv;
+        const int d = (int)(w % D);
+        const int64_t th = w / D;
+        const int64_t t = th / H;
+        const float* src = (part == 0 ? p.k : part == 1 ? p.v : p.q_in) + th * D;
+        float y = src[d];
+        if (ROPE && part != 1) {
+            int32_t pos = p.pos[t];
+            if ((uint64_t)pos >= (uint64_t)p.rope_cap) {
+                flag_error(p.err, kErrBounds);
+                continue;
+            }
+            int jj = d < half ? d : d - half;
+            float2 cs = p.rope[(int64_t)pos * half + jj];
+            float x1 = src[jj], x2 = src[jj + half];
+            y = d < half ? __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y))
+                         : __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
+        }
+        if (part == 2) {
+            p.q_out[th * D + d] = y;
+            continue;
+        }
+        int32_t slot = p.slots[t];
+        if ((uint64_t)slot >= (uint64_t)p.num_slots) {
+            flag_error(p.err, kErrBounds);
+            continue;
+        }
+        int64_t idx = ((int64_t)slot * p.Hkv + (th % H)) * D + d;
+        if constexpr (sizeof(T) == 4) reinterpret_cast<float*>(part == 0 ? p.kpool : p.vpool)[idx] = y;
+        else reinterpret_cast<uint16_t*>(part == 0 ? p.kpool : p.vpool)[idx] = f32_to_bf16(y);
+    }
+}
+
+static bool aligned16(const void* ptr) { return ((uintptr_t)ptr & 15) == 0; }
+
+int launch_append(const AppendParams& p, int dtype, bool rope, cudaStream_t stream) {
+    if (p.n <= 0) return S1KV_OK;
+    if (rope && (p.D % 2)) return set_error(S1KV_EINVAL, "RoPE needs an even head_dim");
+    bool vec = (p.D % 16 == 0) && aligned16(p.k) && aligned16(p.v) && (!p.q_in || (aligned16(p.q_in) && aligned16(p.q_out)));
+    int64_t units = vec ? (2 * p.n * p.Hkv + (rope && p.q_in ? p.n * p.Hq : 0)) * (p.D / 16)
+                        : (2 * p.n * p.Hkv + (rope && p.q_in ? p.n * p.Hq : 0)) * p.D;
+    int grid = (int)std::max<int64_t>(1, std::min<int64_t>((units + 255) / 256, kSMs * 16));
+#define S1KV_APPEND(T, R)                                                                      \
+    (vec ? (void)append_vec_kernel<T, R><<<grid, 256, 0, stream>>>(p)                           \
+         : (void)append_scalar_kernel<T, R><<<grid, 256, 0, stream>>>(p))
+    if (dtype == S1KV_DTYPE_F32) {
+        if (rope) S1KV_APPEND(float, true);
+        else S1KV_APPEND(float, false);
+    } else {
+        if (rope) S1KV_APPEND(uint16_t, true);
+        else S1KV_APPEND(uint16_t, false);
+    }
+#undef S1KV_APPEND
+    g_launches++;
+    S1KV_CUDA(cudaGetLastError());
+    return S1KV_OK;
+}
+
+// ------------------------------------------------------- standalone RoPE --
+__global__ void rope_kernel(const float* __restrict__ x, float* __restrict__ out, const float2* __restrict__ tab,
+                            int64_t cap, int64_t start_pos, int64_t n, int H, int D, int* err) {
+    const int half = D / 2;
+    const int64_t total = n * H * half;
+    for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
+        int j = (int)(u % half);
+        int64_t th = u / half;
+        int64_t pos = start_pos + th / H;
+        if (pos >= cap) {
+            flag_error(err, kErrBounds);
+            continue;
+        }
+        float2 cs = tab[pos * half + j];
+        float x1 = x[th * D + j], x2 = x[th * D + j + half];
+        out[th * D + j] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+        out[th * D + j + half] = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
+    }
+}
+
+int launch_rope(const float* x, float* out, const float2* table, int64_t cap, int64_t start_pos, int64_t n, int32_t H,
+                int32_t D, int* err, cudaStream_t stream) {
+    int64_t total = n * H * (D / 2);
+    if (total <= 0) return S1KV_OK;
+    int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, kSMs * 16));
+    rope_kernel<<<grid, 256, 0, stream>>>(x, out, table, cap, start_pos, n, H, D, err);
+    g_launches++;
+    S1KV_CUDA(cudaGetLastError());
+    return S1KV_OK;
+}
+
+// ---------------------------------------------------------------- gather --
+// get_k / get_v (kv_block_pool.cpp:67-132): token i of the sequence is read
+// from slot table[i / bs] * bs + i % bs and widened to fp32.
+template <typename T>
+__global__ void gather_kernel(const T* __restrict__ pool, const int32_t* __restrict__ trow, int64_t len, int bs,
+                              int row_elems, int32_t max_blocks, float* __restrict__ out, int* err) {
+    const int64_t total = len * row_elems;
+    for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
+        int64_t i = u / row_elems;
+        int e = (int)(u % row_elems);
+        int32_t b = trow[i / bs];
+        if ((uint32_t)b >= (uint32_t)max_blocks) {
+            flag_error(err, kErrBounds);
+            out[u] = 0.0f;
+            continue;
+        }
+        int64_t src = ((int64_t)b * bs + i % bs) * row_elems + e;
+        if constexpr (sizeof(T) == 4) out[u] = reinterpret_cast<const float*>(pool)[src];
+        else out[u] = bf16_to_f32(reinterpret_cast<const uint16_t*>(pool)[src]);
+    }
+}
+
+int launch_gather(s1kv_pool* p, int32_t layer, int32_t row, int64_t len, int which, float* out, cudaStream_t stream) {
+    if (len <= 0) return S1KV_OK;
+    const char* base = (which ? p->v : p->k) + (size_t)layer * p->layer_bytes;
+    const int32_t* trow = p->d_table + (int64_t)row * p->max_bps;
+    int row_elems = p->desc.num_kv_heads * p->desc.head_dim;
+    int64_t total = len * row_elems;
+    int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, kSMs * 16));
+    if (p->desc.dtype == S1KV_DTYPE_F32)
+        gather_kernel<float><<<grid, 256, 0, stream>>>((const float*)base, trow, len, p->desc.block_size, row_elems,
+                                                      (int32_t)p->desc.max_blocks, out, p->d_err);
+    else
+        gather_kernel<uint16_t><<<grid, 256, 0, stream>>>((const uint16_t*)base, trow, len, p->desc.block_size,
+                                                         row_elems, (int32_t)p->desc.max_blocks, out, p->d_err);
+    g_launches++;
+    S1KV_CUDA(cudaGetLastError());
+    return S1KV_OK;
+}
+
+}  // namespace s1kv

@@ -1,0 +1,114 @@
+"""Generates the golden fixtures in this directory by running the
+reference's own CPU implementation (oracle/_ref/libs1ref.so, compiled from
+the reference sources by oracle/Makefile).
+
+    python tests/golden/make_golden.py
+
+Writes:
+  rope.npz        apply_rope outputs (src/nn/RoPE.cpp) for seeded inputs
+  pool_ops.npz    KVBlockPool bookkeeping (status, length, block table)
+                  after every op of seeded op scripts
+  <scenario>.npz  paged-attention outputs and block tables of the scenarios
+                  in scenarios.py (prefill + decode through KVBlockPool,
+                  apply_rope, GQA_attention_paged)
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, HERE)
+
+from oracle import oracle as O  # noqa: E402
+import scenarios as S  # noqa: E402
+
+
+class RefBackend:
+    """One reference KVBlockPool per layer, as src/demo.cpp:56-59 builds."""
+
+    def new_pools(self, layers, H, D, max_blocks, bs, order):
+        self.pools = [O.RefPool(H, D, max_blocks, bs) for _ in range(layers)]
+        self.bs = bs
+        plan = S.remove_trick_plan(max_blocks, order)
+        for p in self.pools:
+            z = np.zeros((bs, H, D), np.float32)
+            for i in range(max_blocks):
+                assert p.append(S.DUMMY_BASE + i, z, z) == 0
+            for i in plan:
+                assert p.remove(S.DUMMY_BASE + i) == 0
+
+    def rope(self, x, pos):
+        return O.ref_apply_rope(x, pos)
+
+    def append(self, layer, seq, k, v):
+        assert self.pools[layer].append(seq, k, v) == 0
+
+    def attention(self, layer, seq, q, Hq):
+        return self.pools[layer].attention(seq, q, Hq)
+
+    def length(self, seq, layer=0):
+        return self.pools[layer].length(seq)
+
+    def table(self, seq):
+        tabs = [p.block_table(seq) for p in self.pools]
+        for t in tabs[1:]:
+            assert np.array_equal(t, tabs[0]), "per-layer tables must agree"
+        return tabs[0]
+
+
+def make_rope():
+    out = {}
+    rng = np.random.default_rng(11)
+    for D in (4, 64, 128):
+        x = rng.standard_normal((3, 2, D), dtype=np.float32)
+        out[f"x_{D}"] = x
+        for pos in (0, 1, 4095, 131071):
+            out[f"out_{D}_{pos}"] = O.ref_apply_rope(x, pos)
+    np.savez_compressed(os.path.join(HERE, "rope.npz"), **out)
+
+
+def make_pool_ops():
+    out = {}
+    for seed in range(4):
+        ops = S.pool_ops(seed)
+        p = O.RefPool(1, 2, 12, 4)
+        rng = np.random.default_rng(100 + seed)
+        status, lengths, tables = [], [], []
+        for kind, seq, n in ops:
+            if kind == "append":
+                k = rng.standard_normal((n, 1, 2), dtype=np.float32)
+                st = p.append(seq, k, k)
+            elif kind == "truncate":
+                st = p.truncate(seq, n)
+            else:
+                st = p.remove(seq)
+            status.append(st)
+            lengths.append(p.length(seq))
+            t = p.block_table(seq)
+            tables.append(-np.ones(12, np.int32) if t is None else np.pad(t, (0, 12 - len(t)), constant_values=-2))
+        out[f"ops_{seed}"] = np.array([[["append", "truncate", "remove"].index(k), s, n] for k, s, n in ops], np.int64)
+        out[f"status_{seed}"] = np.array(status, np.int32)
+        out[f"length_{seed}"] = np.array(lengths, np.int64)
+        out[f"tables_{seed}"] = np.stack(tables)
+    np.savez_compressed(os.path.join(HERE, "pool_ops.npz"), **out)
+
+
+def main():
+    O.build()
+    if not O.ref_available():
+        sys.exit("oracle/_ref/libs1ref.so missing: the reference sources are needed to make fixtures")
+    make_rope()
+    make_pool_ops()
+    for name in S.SCENARIOS:
+        res = S.run_scenario(name, RefBackend())
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **S.flatten(res, name))
+    print("fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()
