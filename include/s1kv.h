@@ -113,6 +113,10 @@ int s1kv_pool_storage(const s1kv_pool* pool, int32_t layer, void** k_base, void*
  * (n_slots * num_kv_heads * head_dim elements of the pool dtype). */
 int s1kv_pool_read(s1kv_pool* pool, int32_t layer, int32_t which, int64_t slot0, int64_t n_slots, void* host_out);
 
+/* s1kv_pool_check for the device error word of CUDA device `device`
+ * (shared by every pool and call on that device). */
+int s1kv_device_check(int device, int32_t* flags_out);
+
 /* Reads and clears the device error word (synchronises the device).  Bit 0:
  * a kernel saw a slot or block id out of range; bit 1: a bounded wait timed
  * out.  Returns S1KV_EDEVICE / S1KV_ETIMEOUT when a bit was set. */
@@ -194,10 +198,12 @@ int s1kv_append(s1kv_pool* pool, int32_t layer, const float* k, const float* v, 
 
 /* Fused RoPE + append.  k is rotated at pos[t] (apply_rope, RoPE.cpp:6-39)
  * and stored with v at slots[t].  When q_in is non-NULL, q_in [n][n_q_heads]
- * [head_dim] is rotated at the same positions into q_out. */
+ * [head_dim] is rotated at the same positions into q_out.  max_pos is an
+ * exclusive bound on the pos values (0 = the longest sequence in the pool);
+ * a position beyond it is skipped and flagged in the device error word. */
 int s1kv_rope_append(s1kv_pool* pool, int32_t layer, const float* q_in, float* q_out, int32_t n_q_heads,
                      const float* k, const float* v, const int32_t* slots, const int32_t* pos, int64_t n,
-                     void* stream);
+                     int64_t max_pos, void* stream);
 
 /* apply_rope(input, start_pos) (RoPE.cpp:6-39) of x [n][n_heads][head_dim]
  * on the current CUDA device: token t rotates at start_pos + t.  theta 0 =

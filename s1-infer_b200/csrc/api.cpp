@@ -358,7 +358,8 @@ int s1kv_append(s1kv_pool* p, int32_t layer, const float* k, const float* v, con
 }
 
 int s1kv_rope_append(s1kv_pool* p, int32_t layer, const float* q_in, float* q_out, int32_t Hq, const float* k,
-                     const float* v, const int32_t* slots, const int32_t* pos, int64_t n, void* stream) {
+                     const float* v, const int32_t* slots, const int32_t* pos, int64_t n, int64_t max_pos,
+                     void* stream) {
     int st = check_pool(p);
     if (!st) st = check_layer(p, layer);
     if (st) return st;
@@ -381,10 +382,13 @@ int s1kv_rope_append(s1kv_pool* p, int32_t layer, const float* q_in, float* q_ou
     ap.Hq = Hq;
     ap.D = p->desc.head_dim;
     ap.err = p->d_err;
-    // Positions are token indices of sequences in this pool, so the longest
-    // sequence length bounds them; the kernel flags anything beyond.
-    ap.rope = rope_table(p->device, p->desc.head_dim, p->desc.rope_theta, std::max<int64_t>(p->max_len_seen, 1),
-                         &ap.rope_cap, (cudaStream_t)stream, &st);
+    // Without an explicit bound the positions are token indices of
+    // sequences in this pool, so the longest sequence bounds them; the
+    // kernel flags anything beyond the table.
+    if (max_pos < 0) return set_error(S1KV_EINVAL, "s1kv_rope_append: negative max_pos");
+    const int64_t bound = max_pos > 0 ? max_pos : std::max<int64_t>(p->max_len_seen, 1);
+    ap.rope = rope_table(p->device, p->desc.head_dim, p->desc.rope_theta, bound, &ap.rope_cap, (cudaStream_t)stream,
+                         &st);
     if (st) return st;
     return launch_append(ap, p->desc.dtype, true, (cudaStream_t)stream);
 }

@@ -504,11 +504,17 @@ int s1kv_pool_storage(const s1kv_pool* p, int32_t layer, void** k, void** v) {
 
 int s1kv_pool_check(s1kv_pool* p, int32_t* flags_out) {
     if (!p || p->host_only) return set_error(S1KV_EINVAL, "s1kv_pool_check: no device pool");
-    S1KV_CUDA(cudaSetDevice(p->device));
+    return s1kv_device_check(p->device, flags_out);
+}
+
+int s1kv_device_check(int device, int32_t* flags_out) {
+    S1KV_CUDA(cudaSetDevice(device));
+    int* word = device_error_word(device);
+    if (!word) return set_error(S1KV_ENOMEM, "s1kv: error word allocation failed");
     S1KV_CUDA(cudaDeviceSynchronize());
     int h = 0;
-    S1KV_CUDA(cudaMemcpy(&h, p->d_err, sizeof(int), cudaMemcpyDeviceToHost));
-    S1KV_CUDA(cudaMemset(p->d_err, 0, sizeof(int)));
+    S1KV_CUDA(cudaMemcpy(&h, word, sizeof(int), cudaMemcpyDeviceToHost));
+    S1KV_CUDA(cudaMemset(word, 0, sizeof(int)));
     if (flags_out) *flags_out = h;
     if (h & kErrTimeout) return set_error(S1KV_ETIMEOUT, "s1kv: a bounded device wait timed out");
     if (h & kErrBounds) return set_error(S1KV_EDEVICE, "s1kv: a kernel saw an out-of-range slot or block");

@@ -82,7 +82,8 @@ SIGNATURES = {
     "s1kv_prefix_load": (C.c_int, [vp, u64, i64, C.c_char_p]),
     "s1kv_flush": (C.c_int, [vp, vp]),
     "s1kv_append": (C.c_int, [vp, i32, vp, vp, vp, i64, vp]),
-    "s1kv_rope_append": (C.c_int, [vp, i32, vp, vp, i32, vp, vp, vp, vp, i64, vp]),
+    "s1kv_rope_append": (C.c_int, [vp, i32, vp, vp, i32, vp, vp, vp, vp, i64, i64, vp]),
+    "s1kv_device_check": (C.c_int, [C.c_int, P(i32)]),
     "s1kv_apply_rope": (C.c_int, [vp, vp, i64, i64, i32, i32, f32, vp]),
     "s1kv_gather": (C.c_int, [vp, i32, u64, i32, vp, vp]),
     "s1kv_cow_copy": (C.c_int, [vp, vp, vp, i64, vp]),
@@ -145,6 +146,13 @@ def _cuda_f32(x, device):
 
 def launch_count():
     return int(lib().s1kv_launch_count())
+
+
+def device_check(device=0):
+    """Reads and clears the device error word; raises S1KVError if set."""
+    f = i32()
+    check(lib().s1kv_device_check(device, C.byref(f)))
+    return f.value
 
 
 # ==================================================================== Pool ==
@@ -282,8 +290,9 @@ class Pool:
         p = torch.as_tensor(pos, dtype=torch.int32).to(self.device)
         q_in = _cuda_f32(q, self.device) if q is not None else None
         q_out = torch.empty_like(q_in) if q_in is not None else None
+        max_pos = int(np.max(np.asarray(pos))) + 1 if len(pos) else 0
         check(self.L.s1kv_rope_append(self.h, layer, _dptr(q_in), _dptr(q_out), q_in.shape[1] if q_in is not None else 0,
-                                      _dptr(k), _dptr(v), _dptr(s), _dptr(p), k.shape[0], _stream()))
+                                      _dptr(k), _dptr(v), _dptr(s), _dptr(p), k.shape[0], max_pos, _stream()))
         return q_out
 
     def gather(self, layer, seq, which):

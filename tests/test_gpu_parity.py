@@ -37,6 +37,17 @@ def host(t):
     return t.detach().cpu().numpy()
 
 
+@pytest.fixture(autouse=True)
+def clean_error_word(s1kv, cuda):
+    """Every test starts with a clear device error word, so a flag left by
+    one test cannot fail another."""
+    try:
+        s1kv.device_check(0)
+    except s1kv.S1KVError:
+        pass
+    yield
+
+
 # ------------------------------------------------------------------ RoPE ---
 
 def test_apply_rope_matches_golden(s1kv, cuda):
