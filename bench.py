@@ -36,7 +36,7 @@ for _p in (ROOT, os.path.join(ROOT, "s1-infer_b200")):
         sys.path.insert(0, _p)
 
 METRIC = "paged decode-attn KV GB/s/GPU (% HBM peak); decode tok/s at 1/2/4/8 B200"
-LAYERS, HQ, HKV, D, BS = 32, 32, 8, 128, 16
+LAYERS, HQ, HKV, D, BS = 32, 32, 8, 128, 16  # LAYERS may be lowered by --layers for profiling cases
 SEQS_PER_GPU = 64
 CTX_LO, CTX_HI, CTX_SEED = 128, 4096, 1
 WORKLOAD = "cfg2: batched ragged paged decode, Llama-3-8B attention shape"
@@ -78,67 +78,72 @@ def decode_bytes(ctx_after, elem):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons of this rank's GPU, sampled every
-    200 ms while running."""
+    """SM clock and clock-event (throttle) reasons of this rank's GPU,
+    polled every 100 ms from a thread through NVML while the timed region
+    runs (nvidia-smi as a fallback)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_S = 0.1
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
 
     def __init__(self, device):
         import torch
-        self.proc = None
-        self.lines = []
-        gid = None
+        self.samples = []
+        self.stop_ev = threading.Event()
+        self.nvml = None
+        pr = torch.cuda.get_device_properties(device)
+        self.bus = "%08X:%02X:%02X.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
         try:
-            pr = torch.cuda.get_device_properties(device)
-            gid = "%08X:%02X:%02X.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+            import pynvml
+            pynvml.nvmlInit()
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(self.bus.encode())
+            self.nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
         except Exception:
-            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-            gid = vis.split(",")[device] if vis else str(device)
-        self.gid = gid
+            self.nvml = None
+
+    def _poll(self):
+        n = self.nvml
+        while not self.stop_ev.is_set():
+            try:
+                sm = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM)
+                try:
+                    rs = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                except AttributeError:
+                    rs = n.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                self.samples.append((sm, rs))
+            except Exception:
+                pass
+            self.stop_ev.wait(self.PERIOD_S)
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gid}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+        if self.nvml:
+            self.t = threading.Thread(target=self._poll, daemon=True)
             self.t.start()
-        except Exception:
-            self.proc = None
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
 
     def stop(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
+        if not self.nvml:
+            return self._smi_once()
+        self.stop_ev.set()
         self.t.join(timeout=2)
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no samples"], "samples": 0}
+        reasons = set()
+        for _, rs in self.samples:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm for sm, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml"}
+
+    def _smi_once(self):
+        try:
+            out = subprocess.run(["nvidia-smi", f"--id={self.bus}", "--query-gpu=clocks.sm,clocks.max.sm",
+                                  "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=10).stdout
+            sm, smax = (float(x) for x in out.strip().split(","))
+            return {"sm_mhz": sm, "sm_max_mhz": smax, "reasons": [], "samples": 1, "source": "nvidia-smi after"}
+        except Exception:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"], "samples": 0}
 
 
 # ----------------------------------------------------------------- ours ---
@@ -332,8 +337,17 @@ def run_ours(args):
     peak, peak_kind = load_peaks()
     res = {}
     for dtype in ("f32", "bf16"):
+        if args.only and dtype != args.only:
+            continue
         res[dtype] = run_variant(s1kv, torch, dtype, share, args.steps, args.warmup, rank, world,
-                                 timed_e2e=True, sample_clocks=(dtype == "f32"))
+                                 timed_e2e=not args.no_e2e, sample_clocks=(dtype == "f32"))
+    if args.only:
+        # profiling case: one variant, no summary line
+        if rank == 0:
+            r = res[args.only]
+            print(json.dumps({"profiling_case": args.only, "layers": LAYERS, "ms_per_step": r["elapsed_ms"] / args.steps,
+                              "avg_launch_ms": r["avg_launch_ms"], "bytes_per_launch": r["bytes_per_launch"]}))
+        return
     h = res["f32"]
     elapsed = max_over_ranks(torch, world, h["elapsed_ms"])
     tokens = sum_over_ranks(torch, world, h["tokens"])
@@ -449,11 +463,15 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="profiling cases only (the bench line uses 32)")
+    ap.add_argument("--only", choices=["f32", "bf16"], help="profiling case: run one storage variant")
+    ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
+    globals()["LAYERS"] = args.layers
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -14,17 +14,21 @@
 //   * one CTA keeps all G query heads of its KV group, so every K/V byte
 //     is read from HBM exactly once per row.
 //   * each warp is an independent worker over tiles warp, warp+NW, ... of
-//     the split.  A tile is one 16-token block; its K rows and V rows for
-//     the kv head are two TMA boxes (16 rows x head_dim) landing in the
-//     warp's ring of NS shared-memory stages, completion tracked by one
-//     mbarrier per stage (bounded waits; a timeout sets the device error
-//     word).  No TMA multicast anywhere.
+//     the split.  A tile is 8 or 16 tokens of one block; its K rows and V
+//     rows for the kv head are two TMA boxes (tile rows x head_dim) landing
+//     in the warp's ring of NS shared-memory stages, completion tracked by
+//     one mbarrier per stage (bounded waits; a timeout sets the device
+//     error word).  Rings are small so 3-4 CTAs (12-16 warps) share an SM.
+//     No TMA multicast anywhere.
 //   * QK: LPT lanes share one token; lane part p reads 16-byte chunks
 //     p, p+LPT, ... of the row, so each quarter-warp phase hits 8 distinct
-//     bank groups.  q stays in registers (G x D/LPT floats).  Partial dots
-//     are combined with log2(LPT) xor-shuffles.
-//   * online softmax per tile in the exp2 domain; PV with lanes over head
-//     dims (D/32 each) and p broadcast by shuffle.
+//     bank groups.  q stays in registers as float pairs and the dot runs on
+//     packed fp32 FMA (__ffma2_rn).  A transpose-reduce leaves each lane
+//     with ONE full (token, head) score, so exponentials are not repeated
+//     across lanes.
+//   * online softmax per tile in the exp2 domain (ex2.approx); PV with
+//     lanes over head dims (D/32 each, packed FMA) and p broadcast from a
+//     small per-warp shared-memory table.
 //   * warps merge through shared memory; multi-split rows write partial
 //     (max, sum, o) and a combine kernel finishes them.
 // Generic path: one warp per query head, one token at a time; used for the
@@ -90,45 +94,6 @@ __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// 16 bytes of storage -> EPC floats.
-template <typename T>
-__device__ __forceinline__ void load_chunk(const T* src, float* x);
-
-template <>
-__device__ __forceinline__ void load_chunk<float>(const float* src, float* x) {
-    float4 a = *reinterpret_cast<const float4*>(src);
-    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-}
-
-template <>
-__device__ __forceinline__ void load_chunk<uint16_t>(const uint16_t* src, float* x) {
-    uint4 a = *reinterpret_cast<const uint4*>(src);
-    x[0] = bf16lo(a.x); x[1] = bf16hi(a.x); x[2] = bf16lo(a.y); x[3] = bf16hi(a.y);
-    x[4] = bf16lo(a.z); x[5] = bf16hi(a.z); x[6] = bf16lo(a.w); x[7] = bf16hi(a.w);
-}
-
-// N consecutive storage elements (N = D/32: 2 or 4) -> floats.
-template <typename T, int N>
-__device__ __forceinline__ void load_vec(const T* src, float* x) {
-    if constexpr (sizeof(T) == 4) {
-        if constexpr (N == 4) {
-            float4 a = *reinterpret_cast<const float4*>(src);
-            x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-        } else {
-            float2 a = *reinterpret_cast<const float2*>(src);
-            x[0] = a.x; x[1] = a.y;
-        }
-    } else {
-        if constexpr (N == 4) {
-            uint2 a = *reinterpret_cast<const uint2*>(src);
-            x[0] = bf16lo(a.x); x[1] = bf16hi(a.x); x[2] = bf16lo(a.y); x[3] = bf16hi(a.y);
-        } else {
-            uint32_t a = *reinterpret_cast<const uint32_t*>(src);
-            x[0] = bf16lo(a); x[1] = bf16hi(a);
-        }
-    }
-}
-
 template <typename T>
 __device__ __forceinline__ float load_elem(const T* src) {
     if constexpr (sizeof(T) == 4) return *reinterpret_cast<const float*>(src);
@@ -136,35 +101,144 @@ __device__ __forceinline__ float load_elem(const T* src) {
 }
 
 // ------------------------------------------------------- configuration ---
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+constexpr int ilog2(int x) { return x <= 1 ? 0 : 1 + ilog2(x / 2); }
+constexpr int pow2ceil(int x) { return x <= 1 ? 1 : 2 * pow2ceil((x + 1) / 2); }
+
+// Tokens per pipeline stage (one TMA box of K and one of V) and stages per
+// warp, by storage type and head dim: the ring of 4 warps fits 3-4 CTAs per
+// SM (12-16 resident warps) while keeping >= 64 KB of loads in flight.
+template <int ELEM, int D>
+struct StageCfg;
+template <> struct StageCfg<4, 128> { static constexpr int kTile = 8, kNS = 2, kMinCtas = 3; };
+template <> struct StageCfg<2, 128> { static constexpr int kTile = 16, kNS = 2, kMinCtas = 3; };
+template <> struct StageCfg<4, 64> { static constexpr int kTile = 16, kNS = 2, kMinCtas = 3; };
+template <> struct StageCfg<2, 64> { static constexpr int kTile = 16, kNS = 3, kMinCtas = 4; };
+
+int decode_tile_rows(int dtype, int D) {
+    if (dtype == S1KV_DTYPE_F32) return D == 128 ? StageCfg<4, 128>::kTile : StageCfg<4, 64>::kTile;
+    return D == 128 ? StageCfg<2, 128>::kTile : StageCfg<2, 64>::kTile;
+}
+
 template <typename T, int D, int G>
 struct DecodeCfg {
-    static constexpr int kBS = 16;                                  // tokens per tile (= block_size)
-    static constexpr int kEPC = 16 / (int)sizeof(T);                // elements per 16-byte chunk
-    static constexpr int kNCH = D / kEPC;                           // chunks per row
-    static constexpr int kLPT = (G * D / 8 > 64 && kNCH >= 16) ? 16 : 8;  // lanes per token (QK)
-    static constexpr int kIT = kNCH / kLPT;                         // chunks per lane per row
-    static constexpr int kDQ = D / kLPT;                            // q dims per lane
-    static constexpr int kTPS = 32 / kLPT;                          // tokens per QK step
-    static constexpr int kSTEPS = kBS / kTPS;                       // QK steps per tile
-    static constexpr int kDPL = D / 32;                             // PV dims per lane
-    static constexpr int kTileBytes = kBS * D * (int)sizeof(T);     // one K (or V) tile
+    using S = StageCfg<(int)sizeof(T), D>;
+    static constexpr int kNV = pow2ceil(G);                           // heads padded to a power of two
+    static constexpr int kH = ilog2(kNV);                             // halving levels of the reduce
+    static constexpr int kEPC = 16 / (int)sizeof(T);                  // elements per 16-byte chunk
+    static constexpr int kNCH = D / kEPC;                             // chunks per row
+    static constexpr int kLPT = (kNV * D / 8 > 64 && kNCH >= 16) ? 16 : 8;  // lanes per token (QK)
+    static constexpr int kIT = kNCH / kLPT;                           // chunks per lane per row
+    static constexpr int kDQ = D / kLPT;                              // q dims per lane per head
+    static constexpr int kTPS = 32 / kLPT;                            // tokens per QK step
+    static constexpr int kTile = S::kTile;                            // tokens per stage
+    static constexpr int kSteps = kTile / kTPS;                       // QK steps per stage
+    static constexpr int kDPL = D / 32;                               // PV dims per lane
+    static constexpr int kTileBytes = kTile * D * (int)sizeof(T);     // one K (or V) box
     static constexpr int kStageBytes = 2 * kTileBytes;
-    static constexpr int kNW = (sizeof(T) == 4 && D == 128) ? 4 : 8;  // warps per CTA
-    static constexpr int kNS = (kStageBytes <= 4096) ? 4 : 3;         // stages per warp
-    static constexpr int kSmem = kNW * kNS * kStageBytes + kNW * kNS * 8;
+    static constexpr int kNW = 4;                                     // warps per CTA
+    static constexpr int kNS = S::kNS;                                // stages per warp
+    static constexpr int kPFloats = (kTile * kNV + kNV + 3) / 4 * 4;  // p[tile][head] + corr[head]
+    static constexpr int kRing = kNW * kNS * kStageBytes;
+    static constexpr int kSmem = kRing + kNW * kPFloats * 4 + kNW * kNS * 8;
     static_assert(kNCH % kLPT == 0, "chunks must split evenly over lanes");
     static_assert(kLPT >= 8, "a quarter-warp phase must read 8 distinct chunks");
-    static_assert(kNW * kNS * kStageBytes >= kNW * G * (D + 2) * 4, "merge area must fit in the stage ring");
+    static_assert((1 << kH) <= kLPT, "one halving level per lane bit");
+    static_assert(kTile % kTPS == 0 && 16 % kTile == 0, "tiles are whole QK steps inside one block");
+    static_assert(kRing >= kNW * kNV * (D + 2) * 4, "merge area must fit in the stage ring");
+    static_assert((kPFloats * 4) % 16 == 0, "p area keeps 16-byte alignment");
 };
+
+// Sums NV per-lane partial dots over the LPT lanes of a token so that each
+// lane ends with ONE full dot: halving levels trade half of the values with
+// the partner lane (one shuffle per traded value), then plain butterflies
+// finish.  The lane keeps head index sum_i hi_i * (NV >> (i+1)), where hi_i
+// is the lane bit (LPT >> (i+1)).
+template <int NV, int LPT>
+__device__ __forceinline__ float reduce_transpose(float (&a)[NV], int lane) {
+    constexpr int H = ilog2(NV);
+#pragma unroll
+    for (int i = 0; i < H; i++) {
+        const int off = LPT >> (i + 1);
+        const int half = NV >> (i + 1);
+        const bool hi = (lane & off) != 0;
+#pragma unroll
+        for (int x = 0; x < half; x++) {
+            const float send = hi ? a[x] : a[x + half];
+            const float keep = hi ? a[x + half] : a[x];
+            a[x] = keep + __shfl_xor_sync(kFull, send, off);
+        }
+    }
+#pragma unroll
+    for (int off = LPT >> (H + 1); off >= 1; off >>= 1) a[0] += __shfl_xor_sync(kFull, a[0], off);
+    return a[0];
+}
+
+template <int NV, int LPT>
+__device__ __forceinline__ int reduced_head(int lane) {
+    constexpr int H = ilog2(NV);
+    int g = 0;
+#pragma unroll
+    for (int i = 0; i < H; i++) g |= ((lane & (LPT >> (i + 1))) ? 1 : 0) << (H - 1 - i);
+    return g;
+}
+
+// 16 bytes of storage -> EPC/2 float pairs.
+template <typename T>
+__device__ __forceinline__ void load_pairs(const T* src, float2* x);
+
+template <>
+__device__ __forceinline__ void load_pairs<float>(const float* src, float2* x) {
+    float4 a = *reinterpret_cast<const float4*>(src);
+    x[0] = make_float2(a.x, a.y);
+    x[1] = make_float2(a.z, a.w);
+}
+
+template <>
+__device__ __forceinline__ void load_pairs<uint16_t>(const uint16_t* src, float2* x) {
+    uint4 a = *reinterpret_cast<const uint4*>(src);
+    x[0] = make_float2(bf16lo(a.x), bf16hi(a.x));
+    x[1] = make_float2(bf16lo(a.y), bf16hi(a.y));
+    x[2] = make_float2(bf16lo(a.z), bf16hi(a.z));
+    x[3] = make_float2(bf16lo(a.w), bf16hi(a.w));
+}
+
+// N = D/32 consecutive storage elements (2 or 4) -> N/2 float pairs.
+template <typename T, int N>
+__device__ __forceinline__ void load_vpairs(const T* src, float2* x) {
+    if constexpr (sizeof(T) == 4) {
+        if constexpr (N == 4) {
+            float4 a = *reinterpret_cast<const float4*>(src);
+            x[0] = make_float2(a.x, a.y);
+            x[1] = make_float2(a.z, a.w);
+        } else {
+            x[0] = *reinterpret_cast<const float2*>(src);
+        }
+    } else {
+        if constexpr (N == 4) {
+            uint2 a = *reinterpret_cast<const uint2*>(src);
+            x[0] = make_float2(bf16lo(a.x), bf16hi(a.x));
+            x[1] = make_float2(bf16lo(a.y), bf16hi(a.y));
+        } else {
+            uint32_t a = *reinterpret_cast<const uint32_t*>(src);
+            x[0] = make_float2(bf16lo(a), bf16hi(a));
+        }
+    }
+}
 
 // ------------------------------------------------------------- decode ----
 template <typename T, int D, int G>
-__global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, 1)
+__global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, G>::S::kMinCtas)
     decode_tma_kernel(const __grid_constant__ AttnParams p, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV) {
     using C = DecodeCfg<T, D, G>;
-    constexpr int NW = C::kNW, NS = C::kNS, LPT = C::kLPT, IT = C::kIT, EPC = C::kEPC, TPS = C::kTPS,
-                  STEPS = C::kSTEPS, DPL = C::kDPL, DQ = C::kDQ;
+    constexpr int NW = C::kNW, NS = C::kNS, NV = C::kNV, LPT = C::kLPT, IT = C::kIT, EPC = C::kEPC,
+                  TPS = C::kTPS, STEPS = C::kSteps, DPL = C::kDPL, DQ = C::kDQ, TILE = C::kTile;
     extern __shared__ __align__(1024) uint8_t smem[];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -173,71 +247,76 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, 1)
     const RowMeta rm = p.rows[item.row];
     const int tok0 = item.split * p.split_tokens;
     const int tok1 = min(tok0 + p.split_tokens, rm.kv_len);
-    const int n_tiles = (tok1 - tok0 + 15) >> 4;
+    const int n_tiles = (tok1 - tok0 + TILE - 1) / TILE;
     const int my_tiles = n_tiles > warp ? (n_tiles - warp + NW - 1) / NW : 0;
-    const int32_t* tab = p.table + (int64_t)rm.table_row * p.max_bps + (tok0 >> 4);
+    const int32_t* tab = p.table + (int64_t)rm.table_row * p.max_bps;
 
     uint8_t* ring = smem + warp * NS * C::kStageBytes;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + NW * NS * C::kStageBytes) + warp * NS;
+    float* Ps = reinterpret_cast<float*>(smem + C::kRing) + warp * C::kPFloats;  // [TILE][NV]
+    float* Cs = Ps + TILE * NV;                                                 // [NV]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::kRing + NW * C::kPFloats * 4) + warp * NS;
 
-    // Block ids of this warp's first 32 tiles, one per lane.
-    int32_t my_blk = 0;
-    if (lane < my_tiles) my_blk = tab[warp + lane * NW];
-    if (lane < my_tiles && (uint32_t)my_blk >= (uint32_t)p.max_blocks) {
-        atomicOr(p.err, kErrBounds);
-        my_blk = p.max_blocks;  // TMA zero-fills boxes that start out of range
-    }
+    // TMA row coordinate of this warp's k-th tile for k = lane (first 32).
+    auto tile_row = [&](int k, int& row) -> bool {
+        const int base = tok0 + (warp + k * NW) * TILE;
+        const int32_t blk = tab[base >> 4];
+        if ((uint32_t)blk >= (uint32_t)p.max_blocks) {
+            row = p.max_blocks * 16;  // out of range: TMA zero-fills the box
+            return false;
+        }
+        row = blk * 16 + (base & 15);
+        return true;
+    };
+    int my_row = 0;
+    if (lane < my_tiles && !tile_row(lane, my_row)) atomicOr(p.err, kErrBounds);
     if (lane == 0) {
         for (int s = 0; s < NS; s++) mbar_init(&bar[s], 1);
         fence_barrier_init();
     }
     __syncwarp();
 
-    auto issue = [&](int k, int32_t blk) {
+    auto issue = [&](int k, int row) {
         const int s = k % NS;
         uint8_t* dst = ring + s * C::kStageBytes;
         mbar_expect_tx(&bar[s], C::kStageBytes);
-        tma_load_4d(dst, &tmK, &bar[s], 0, h, blk * 16, p.layer);
-        tma_load_4d(dst + C::kTileBytes, &tmV, &bar[s], 0, h, blk * 16, p.layer);
+        tma_load_4d(dst, &tmK, &bar[s], 0, h, row, p.layer);
+        tma_load_4d(dst + C::kTileBytes, &tmV, &bar[s], 0, h, row, p.layer);
     };
     {
         const int pre = min(NS, my_tiles);
         for (int k = 0; k < pre; k++) {
-            int32_t blk = __shfl_sync(kFull, my_blk, k);
-            if (lane == 0) issue(k, blk);
+            const int row = __shfl_sync(kFull, my_row, k);
+            if (lane == 0) issue(k, row);
         }
     }
 
-    // q for the G heads of this group: lane part `pp` holds chunks pp,
-    // pp+LPT, ... of every head.
+    // q of the group's heads (padded heads are zero): lane part pp holds
+    // chunks pp, pp+LPT, ... of each head as float pairs.
     const int pp = lane % LPT;
     const int tl = lane / LPT;
-    float qr[G][DQ];
+    const int my_g = reduced_head<NV, LPT>(lane);
+    float2 q2[NV][DQ / 2];
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-        const float* qrow = p.q + ((int64_t)item.row * p.Hq + h * G + g) * D;
+    for (int g = 0; g < NV; g++) {
+        const float* qrow = p.q + ((int64_t)item.row * p.Hq + h * G + (g < G ? g : 0)) * D;
 #pragma unroll
         for (int it = 0; it < IT; it++) {
             const float4* src = reinterpret_cast<const float4*>(qrow + (it * LPT + pp) * EPC);
 #pragma unroll
             for (int e4 = 0; e4 < EPC / 4; e4++) {
-                float4 v = __ldg(src + e4);
-                qr[g][it * EPC + e4 * 4 + 0] = v.x;
-                qr[g][it * EPC + e4 * 4 + 1] = v.y;
-                qr[g][it * EPC + e4 * 4 + 2] = v.z;
-                qr[g][it * EPC + e4 * 4 + 3] = v.w;
+                float4 v = g < G ? __ldg(src + e4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                q2[g][(it * EPC + e4 * 4) / 2] = make_float2(v.x, v.y);
+                q2[g][(it * EPC + e4 * 4) / 2 + 1] = make_float2(v.z, v.w);
             }
         }
     }
 
-    float m[G], l[G], o[G][DPL];
+    float m = -INFINITY, l = 0.0f;  // running max / sum of head my_g (this lane's tokens)
+    float2 o2[NV][DPL / 2];
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-        m[g] = -INFINITY;
-        l[g] = 0.0f;
+    for (int g = 0; g < NV; g++)
 #pragma unroll
-        for (int d = 0; d < DPL; d++) o[g][d] = 0.0f;
-    }
+        for (int d = 0; d < DPL / 2; d++) o2[g][d] = make_float2(0.f, 0.f);
 
     bool failed = false;
     int consumed = 0;
@@ -249,88 +328,88 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, 1)
         }
         consumed = k + 1;
         const T* Ks = reinterpret_cast<const T*>(ring + s * C::kStageBytes);
-        const T* Vs = Ks + 16 * D;
-        const int base = tok0 + (warp + k * NW) * 16;
-        const int valid = min(16, tok1 - base);
+        const T* Vs = Ks + TILE * D;
+        const int base = tok0 + (warp + k * NW) * TILE;
+        const int valid = min(TILE, tok1 - base);
 
-        // ---- scores for the tile ----
-        float sc[STEPS][G];
+        // ---- scores: one (token, head) per lane per step ----
+        float sc[STEPS];
 #pragma unroll
         for (int j = 0; j < STEPS; j++) {
             const int t = j * TPS + tl;
             const T* krow = Ks + t * D;
-            float acc[G];
+            float2 acc2[NV];
 #pragma unroll
-            for (int g = 0; g < G; g++) acc[g] = 0.0f;
+            for (int g = 0; g < NV; g++) acc2[g] = make_float2(0.f, 0.f);
 #pragma unroll
             for (int it = 0; it < IT; it++) {
-                float kf[EPC];
-                load_chunk<T>(krow + (it * LPT + pp) * EPC, kf);
+                float2 kf[EPC / 2];
+                load_pairs<T>(krow + (it * LPT + pp) * EPC, kf);
 #pragma unroll
-                for (int g = 0; g < G; g++)
+                for (int g = 0; g < NV; g++)
 #pragma unroll
-                    for (int e = 0; e < EPC; e++) acc[g] = fmaf(qr[g][it * EPC + e], kf[e], acc[g]);
+                    for (int e = 0; e < EPC / 2; e++) acc2[g] = __ffma2_rn(q2[g][it * EPC / 2 + e], kf[e], acc2[g]);
             }
+            float acc[NV];
 #pragma unroll
-            for (int off = LPT / 2; off >= 1; off >>= 1)
-#pragma unroll
-                for (int g = 0; g < G; g++) acc[g] += __shfl_xor_sync(kFull, acc[g], off);
-#pragma unroll
-            for (int g = 0; g < G; g++) sc[j][g] = (t < valid) ? acc[g] * p.scale_log2 : -INFINITY;
+            for (int g = 0; g < NV; g++) acc[g] = acc2[g].x + acc2[g].y;
+            const float dot = reduce_transpose<NV, LPT>(acc, lane);
+            sc[j] = (t < valid) ? dot * p.scale_log2 : -INFINITY;
         }
 
-        // ---- online softmax update ----
-        float corr[G];
+        // ---- online softmax for head my_g ----
+        float mx = sc[0];
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-            float mx = sc[0][g];
+        for (int j = 1; j < STEPS; j++) mx = fmaxf(mx, sc[j]);
 #pragma unroll
-            for (int j = 1; j < STEPS; j++) mx = fmaxf(mx, sc[j][g]);
+        for (int off = LPT; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
+        const float mn = fmaxf(m, mx);
+        const float corr = ex2(m - mn);
+        m = mn;
+        float ls = 0.0f;
 #pragma unroll
-            for (int off = LPT; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
-            const float mn = fmaxf(m[g], mx);
-            corr[g] = exp2f(m[g] - mn);
-            m[g] = mn;
-            float ls = 0.0f;
-#pragma unroll
-            for (int j = 0; j < STEPS; j++) {
-                sc[j][g] = exp2f(sc[j][g] - mn);
-                ls += sc[j][g];
-            }
-            l[g] = fmaf(l[g], corr[g], ls);
-#pragma unroll
-            for (int d = 0; d < DPL; d++) o[g][d] *= corr[g];
+        for (int j = 0; j < STEPS; j++) {
+            const float pj = ex2(sc[j] - mn);
+            ls += pj;
+            Ps[(j * TPS + tl) * NV + my_g] = pj;
         }
+        l = fmaf(l, corr, ls);
+        if (tl == 0) Cs[my_g] = corr;
+        __syncwarp();
 
-        // ---- PV ----
+        // ---- PV: lanes over head dims, p broadcast from shared memory ----
+        float cg[NV];
 #pragma unroll
-        for (int u = 0; u < 16; u++) {
+        for (int g = 0; g < NV; g++) cg[g] = Cs[g];
+#pragma unroll
+        for (int g = 0; g < NV; g++)
+#pragma unroll
+            for (int d = 0; d < DPL / 2; d++) o2[g][d] = __fmul2_rn(o2[g][d], make_float2(cg[g], cg[g]));
+#pragma unroll
+        for (int u = 0; u < TILE; u++) {
             if (u < valid) {
-                float vf[DPL];
-                load_vec<T, DPL>(Vs + u * D + lane * DPL, vf);
+                float2 vf[DPL / 2];
+                load_vpairs<T, DPL>(Vs + u * D + lane * DPL, vf);
+                float pu[NV];
 #pragma unroll
-                for (int g = 0; g < G; g++) {
-                    const float pv = __shfl_sync(kFull, sc[u / TPS][g], (u % TPS) * LPT);
+                for (int g = 0; g < NV; g++) pu[g] = Ps[u * NV + g];
 #pragma unroll
-                    for (int d = 0; d < DPL; d++) o[g][d] = fmaf(pv, vf[d], o[g][d]);
-                }
+                for (int g = 0; g < NV; g++)
+#pragma unroll
+                    for (int d = 0; d < DPL / 2; d++) o2[g][d] = __ffma2_rn(make_float2(pu[g], pu[g]), vf[d], o2[g][d]);
             }
         }
         __syncwarp();
         if (k + NS < my_tiles) {
-            int32_t blk = __shfl_sync(kFull, my_blk, (k + NS) & 31);
+            int row = __shfl_sync(kFull, my_row, (k + NS) & 31);
             if (k + NS >= 32) {
-                // Tiles past the 32 prefetched ids (splits longer than
-                // 32 * NW tiles): read the id directly.
-                blk = tab[warp + (k + NS) * NW];
-                if ((uint32_t)blk >= (uint32_t)p.max_blocks) {
-                    if (lane == 0) atomicOr(p.err, kErrBounds);
-                    blk = p.max_blocks;
-                }
+                // Past the 32 prefetched rows (splits longer than 32 tiles per
+                // warp): look the block up directly.
+                if (!tile_row(k + NS, row) && lane == 0) atomicOr(p.err, kErrBounds);
             }
             if (lane == 0) {
                 fence_proxy_async();
-                issue(k + NS, blk);
+                issue(k + NS, row);
             }
         }
     }
@@ -340,33 +419,31 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, 1)
         if (lane == 0) atomicOr(p.err, kErrTimeout);
         const int issued = min(my_tiles, consumed + NS);
         for (int k = consumed + 1; k < issued; k++) mbar_wait_bounded(&bar[k % NS], (uint32_t)((k / NS) & 1));
+        m = -INFINITY;
+        l = 0.0f;
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-            m[g] = -INFINITY;
-            l[g] = 0.0f;
+        for (int g = 0; g < NV; g++)
 #pragma unroll
-            for (int d = 0; d < DPL; d++) o[g][d] = 0.0f;
-        }
+            for (int d = 0; d < DPL / 2; d++) o2[g][d] = make_float2(0.f, 0.f);
     }
 
-    // Per-warp totals: l summed over token lanes (part lanes hold copies).
+    // Sum l of head my_g over the token lanes (lanes inside one token group
+    // hold copies).
 #pragma unroll
-    for (int g = 0; g < G; g++)
-#pragma unroll
-        for (int off = LPT; off < 32; off <<= 1) l[g] += __shfl_xor_sync(kFull, l[g], off);
+    for (int off = LPT; off < 32; off <<= 1) l += __shfl_xor_sync(kFull, l, off);
 
     // ---- merge the NW warps through shared memory (aliases the rings) ----
     __syncthreads();
-    float* mo = reinterpret_cast<float*>(smem);            // [NW][G][D]
-    float* mml = mo + NW * G * D;                           // [NW][G][2]
+    float* mo = reinterpret_cast<float*>(smem);   // [NW][NV][D]
+    float* mml = mo + NW * NV * D;                 // [NW][NV][2]
 #pragma unroll
-    for (int g = 0; g < G; g++) {
+    for (int g = 0; g < NV; g++)
 #pragma unroll
-        for (int d = 0; d < DPL; d++) mo[(warp * G + g) * D + lane * DPL + d] = o[g][d];
-        if (lane == 0) {
-            mml[(warp * G + g) * 2] = m[g];
-            mml[(warp * G + g) * 2 + 1] = l[g];
-        }
+        for (int d = 0; d < DPL / 2; d++)
+            *reinterpret_cast<float2*>(&mo[(warp * NV + g) * D + lane * DPL + 2 * d]) = o2[g][d];
+    if (tl == 0) {
+        mml[(warp * NV + my_g) * 2] = m;
+        mml[(warp * NV + my_g) * 2 + 1] = l;
     }
     __syncthreads();
     const int64_t part = (int64_t)(rm.part_off + item.split) * p.Hkv + h;
@@ -374,14 +451,14 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, 1)
         const int g = idx / D, d = idx % D;
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < NW; w++) M = fmaxf(M, mml[(w * G + g) * 2]);
+        for (int w = 0; w < NW; w++) M = fmaxf(M, mml[(w * NV + g) * 2]);
         float L = 0.0f, O = 0.0f;
 #pragma unroll
         for (int w = 0; w < NW; w++) {
-            const float mw = mml[(w * G + g) * 2];
-            const float f = (mw == -INFINITY) ? 0.0f : exp2f(mw - M);
-            L = fmaf(mml[(w * G + g) * 2 + 1], f, L);
-            O = fmaf(mo[(w * G + g) * D + d], f, O);
+            const float mw = mml[(w * NV + g) * 2];
+            const float f = (mw == -INFINITY) ? 0.0f : ex2(mw - M);
+            L = fmaf(mml[(w * NV + g) * 2 + 1], f, L);
+            O = fmaf(mo[(w * NV + g) * D + d], f, O);
         }
         if (rm.n_split == 1) {
             p.out[((int64_t)item.row * p.Hq + h * G + g) * D + d] = O / L;
@@ -412,7 +489,7 @@ __global__ void combine_kernel(const AttnParams p, int G) {
         for (int s = 0; s < rm.n_split; s++) {
             const int64_t part = (int64_t)(rm.part_off + s) * p.Hkv + h;
             const float ms = p.part_ml[(part * G + g) * 2];
-            const float f = (ms == -INFINITY) ? 0.0f : exp2f(ms - M);
+            const float f = (ms == -INFINITY) ? 0.0f : ex2(ms - M);
             L = fmaf(p.part_ml[(part * G + g) * 2 + 1], f, L);
             O = fmaf(p.part_o[(part * G + g) * D + d], f, O);
         }
@@ -490,7 +567,11 @@ bool tma_attention_supported(int dtype, int D, int G, int block_size) {
     return block_size == 16 && (D == 64 || D == 128) && (G == 1 || G == 2 || G == 4 || G == 7 || G == 8);
 }
 
-int tma_warps_per_cta(int dtype, int D) { return (dtype == S1KV_DTYPE_F32 && D == 128) ? 4 : 8; }
+int tma_warps_per_cta(int dtype, int D) {
+    (void)dtype;
+    (void)D;
+    return 4;
+}
 
 template <typename T, int D, int G>
 static int launch_decode_t(s1kv_pool* pool, const AttnParams& p, cudaStream_t stream) {
@@ -554,7 +635,8 @@ int launch_attention(s1kv_pool* pool, const AttnParams& p, int dtype, cudaStream
 
 // --------------------------------------------------------- tensor maps ---
 // One 4-D map per storage tensor: (head_dim, kv head, slot, layer), box
-// (head_dim, 1, 16, 1): one KV head's 16 rows of one block.  No swizzle:
+// (head_dim, 1, tile, 1): one KV head's rows of one decode tile (8 or 16
+// tokens of one block).  No swizzle:
 // the kernels' chunk assignment is already conflict-free.
 int make_tensor_maps(s1kv_pool* p) {
     p->tmap_ok = false;
@@ -576,7 +658,7 @@ int make_tensor_maps(s1kv_pool* p) {
                           (cuuint64_t)p->desc.num_layers};
     cuuint64_t strides[3] = {D * e, (cuuint64_t)p->desc.num_kv_heads * D * e,
                              (cuuint64_t)p->num_slots * p->desc.num_kv_heads * D * e};
-    cuuint32_t box[4] = {(cuuint32_t)D, 1, 16, 1};
+    cuuint32_t box[4] = {(cuuint32_t)D, 1, (cuuint32_t)decode_tile_rows(p->desc.dtype, D), 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     for (int which = 0; which < 2; which++) {
         CUresult r = encode(which ? &p->tmap_v : &p->tmap_k, dt, 4, which ? (void*)p->v : (void*)p->k, dims, strides,

@@ -98,13 +98,15 @@ void Stager::destroy() {
     }
 }
 
+// Grows geometrically (at least 2x, at least 16 MB) so that a workload whose
+// size creeps up step by step reallocates a handful of times, not per step.
 int DevBuf::ensure(size_t bytes) {
     if (cap >= bytes) return S1KV_OK;
     S1KV_CUDA(cudaDeviceSynchronize());
     if (p) cudaFree(p);
     p = nullptr;
+    size_t c = std::max<size_t>({bytes + bytes / 4, 2 * cap, size_t(16) << 20});
     cap = 0;
-    size_t c = std::max<size_t>(bytes, 1 << 20);
     S1KV_CUDA(cudaMalloc(&p, c));
     cap = c;
     return S1KV_OK;
