@@ -195,11 +195,13 @@ def run_variant(s1kv, torch, dtype, ctx, steps, warmup, rank, world, timed_e2e, 
         clocks.start()
     launches0 = s1kv.launch_count()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push(f"timed_decode_{dtype}")  # ncu --nvtx-include filters the launch list on it
     t0.record()
     for i in range(steps):
         step(evs[i])
     t1.record()
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     launches = s1kv.launch_count() - launches0
     clk = clocks.stop() if clocks else None
     elapsed_ms = t0.elapsed_time(t1)

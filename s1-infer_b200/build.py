@@ -91,9 +91,11 @@ def build(verbose_ptxas=False, force=False, jobs=None):
         for dp, _, fs in os.walk(os.path.join(SHIM, "include")):
             shim_hdrs += [os.path.join(dp, f) for f in fs if f.endswith(".h")]
         if force or _stale(SHIM_LIB, shim_srcs + shim_hdrs + [LIB]):
-            _run(["g++"] + HOST_FLAGS + ["-shared", "-I", os.path.join(SHIM, "include"), "-I",
-                                          os.path.join(ROOT, "include"), "-o", SHIM_LIB] + shim_srcs +
-                 ["-L", LIBDIR, "-ls1kv", "-Wl,-rpath,$ORIGIN"])
+            _run(["g++"] + HOST_FLAGS +
+                 ["-shared", "-I", os.path.join(SHIM, "include"), "-I", os.path.join(CUDA, "include"),
+                  "-I", os.path.join(ROOT, "include"), "-o", SHIM_LIB] + shim_srcs +
+                 ["-L", LIBDIR, "-ls1kv", "-L", os.path.join(CUDA, "lib64"), "-lcudart", "-Wl,--no-undefined",
+                  "-Wl,-rpath,$ORIGIN", "-Wl,-rpath," + os.path.join(CUDA, "lib64")])
     return "\n".join(l for l in logs if l.strip())
 
 
