@@ -227,6 +227,44 @@ int s1kv_cow_copy(s1kv_pool* pool, const int32_t* src, const int32_t* dst, int64
 int s1kv_attention(s1kv_pool* pool, int32_t layer, const uint64_t* seqs, const int32_t* q_lens, int32_t n_seqs,
                    const float* q, float* out, int32_t n_q_heads, void* stream);
 
+/* Decode attention that allocates nothing.  No counterpart in the reference:
+ * this is an extra entry point of this library.
+ *
+ * For callers that cannot allocate device memory where attention runs -- a
+ * plugin called from an inference server's execution step (the server owns
+ * all device memory and forbids allocation there), a latency-critical decode
+ * loop that must not block on or fail in the allocator, code with a memory
+ * budget fixed up front.  It computes what s1kv_batch_attention computes for
+ * q_len 1 per sequence, from caller-owned buffers only:
+ *   k_cache, v_cache  one layer's storage [num_slots][num_kv_heads][head_dim]
+ *                     in `dtype` (e.g. from s1kv_pool_storage), 16-byte aligned
+ *   block_tables      device int32 [n_seqs][max_blocks_per_seq]: physical
+ *                     block ids of sequence i in row i
+ *   seq_lens          device int32 [n_seqs], each in [1, max_seq_len]
+ *   q, out            device fp32 [n_seqs][n_q_heads][head_dim]
+ * block_size must be 16, head_dim 64 or 128, n_q_heads / num_kv_heads one of
+ * 1, 2, 4, 7, 8, and max_seq_len <= max_blocks_per_seq * 16.
+ *
+ * Its scratch (split-K partial results, row metadata, work list) is one
+ * fixed 8 MiB array in device memory that every GPU which loads this
+ * library holds until the process exits; the work list is planned on the
+ * device.  The call issues no cudaMalloc, cudaFree or other allocating
+ * routine.  A call whose sizes need more than 8 MiB (about n_seqs x
+ * ceil(max_seq_len / split) x num_kv_heads x (n_q_heads / num_kv_heads) x
+ * (head_dim + 2) x 4 bytes) returns S1KV_EINVAL with the sizes in
+ * s1kv_last_error().  The first call on a device does a one-time set-up
+ * (looks up the array's device address and clears its error word), so make
+ * that first call before any stream capture.  Every call reuses the same
+ * array, which keeps the last call's contents: calls that overlap on the
+ * GPU (other streams, other host threads) race and must be serialised by
+ * the caller.  Sequence lengths outside [1, max_seq_len] are recorded in the
+ * array's error word and their output rows are unspecified. */
+int s1kv_decode_attention_noalloc(const void* k_cache, const void* v_cache, int32_t dtype, int64_t num_slots,
+                                  int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                  const int32_t* block_tables, int32_t max_blocks_per_seq, const int32_t* seq_lens,
+                                  int32_t n_seqs, int32_t max_seq_len, const float* q, float* out,
+                                  int32_t n_q_heads, void* stream);
+
 /* GQA_attention (attention.cpp:13-126) over contiguous device K/V
  * [kv_len][n_kv_heads][head_dim] fp32. */
 int s1kv_attention_contig(const float* q, const float* k, const float* v, int64_t q_len, int64_t kv_len,

@@ -671,3 +671,71 @@ int make_tensor_maps(s1kv_pool* p) {
 }
 
 }  // namespace s1kv
+
+// ------------------------------------------ caller-supplied storage path ---
+// Helpers for the no-allocation entry point (noalloc.cu): tensor maps over
+// one layer of caller-owned K/V storage, and a launcher that takes them
+// instead of a pool's.
+
+namespace s1kv {
+
+int encode_kv_maps(const void* k, const void* v, int dtype, int Hkv, int D, int64_t num_slots, CUtensorMap* tk,
+                   CUtensorMap* tv) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    S1KV_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !fn) return set_error(S1KV_ECUDA, "s1kv: cuTensorMapEncodeTiled unavailable");
+    auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    const cuuint64_t e = dtype == S1KV_DTYPE_F32 ? 4 : 2;
+    const CUtensorMapDataType dt =
+        dtype == S1KV_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)Hkv, (cuuint64_t)num_slots, 1};
+    cuuint64_t strides[3] = {D * e, (cuuint64_t)Hkv * D * e, (cuuint64_t)num_slots * Hkv * D * e};
+    cuuint32_t box[4] = {(cuuint32_t)D, 1, (cuuint32_t)decode_tile_rows(dtype, D), 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    for (int which = 0; which < 2; which++) {
+        CUresult r = encode(which ? tv : tk, dt, 4, const_cast<void*>(which ? v : k), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return set_error(S1KV_EINVAL, "s1kv: tensor map over the K/V storage rejected (%d)", (int)r);
+    }
+    return S1KV_OK;
+}
+
+template <typename T, int D, int G>
+static int launch_with_maps_t(const AttnParams& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream) {
+    using C = DecodeCfg<T, D, G>;
+    S1KV_CUDA(cudaFuncSetAttribute(decode_tma_kernel<T, D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+    decode_tma_kernel<T, D, G><<<dim3((unsigned)p.n_items, (unsigned)p.Hkv), C::kNW * 32, C::kSmem, stream>>>(p, tk, tv);
+    g_launches++;
+    S1KV_CUDA(cudaGetLastError());
+    combine_kernel<<<dim3((unsigned)p.n_rows, (unsigned)p.Hkv), 128, 0, stream>>>(p, G);
+    g_launches++;
+    S1KV_CUDA(cudaGetLastError());
+    return S1KV_OK;
+}
+
+template <typename T, int D>
+static int launch_with_maps_g(const AttnParams& p, const CUtensorMap& tk, const CUtensorMap& tv, int G,
+                              cudaStream_t stream) {
+    switch (G) {
+        case 1: return launch_with_maps_t<T, D, 1>(p, tk, tv, stream);
+        case 2: return launch_with_maps_t<T, D, 2>(p, tk, tv, stream);
+        case 4: return launch_with_maps_t<T, D, 4>(p, tk, tv, stream);
+        case 7: return launch_with_maps_t<T, D, 7>(p, tk, tv, stream);
+        case 8: return launch_with_maps_t<T, D, 8>(p, tk, tv, stream);
+        default: return set_error(S1KV_EINVAL, "decode: unsupported group size %d", G);
+    }
+}
+
+int launch_decode_with_maps(const AttnParams& p, const CUtensorMap& tk, const CUtensorMap& tv, int dtype,
+                            cudaStream_t stream) {
+    const int G = p.Hq / p.Hkv;
+    if (dtype == S1KV_DTYPE_F32)
+        return p.D == 128 ? launch_with_maps_g<float, 128>(p, tk, tv, G, stream)
+                          : launch_with_maps_g<float, 64>(p, tk, tv, G, stream);
+    return p.D == 128 ? launch_with_maps_g<uint16_t, 128>(p, tk, tv, G, stream)
+                      : launch_with_maps_g<uint16_t, 64>(p, tk, tv, G, stream);
+}
+
+}  // namespace s1kv

@@ -227,3 +227,13 @@ int tma_warps_per_cta(int dtype, int D);
 int make_tensor_maps(s1kv_pool* pool);
 
 }  // namespace s1kv
+
+namespace s1kv {
+// Caller-supplied-storage variants (no pool): used by the no-allocation
+// entry point.
+int decode_tile_rows(int dtype, int D);
+int encode_kv_maps(const void* k, const void* v, int dtype, int Hkv, int D, int64_t num_slots, CUtensorMap* tk,
+                   CUtensorMap* tv);
+int launch_decode_with_maps(const AttnParams& p, const CUtensorMap& tk, const CUtensorMap& tv, int dtype,
+                            cudaStream_t stream);
+}  // namespace s1kv

@@ -89,6 +89,8 @@ SIGNATURES = {
     "s1kv_cow_copy": (C.c_int, [vp, vp, vp, i64, vp]),
     "s1kv_attention": (C.c_int, [vp, i32, P(u64), P(i32), i32, vp, vp, i32, vp]),
     "s1kv_attention_contig": (C.c_int, [vp, vp, vp, i64, i64, i32, i32, i32, vp, vp]),
+    "s1kv_decode_attention_noalloc": (C.c_int, [vp, vp, i32, i64, i32, i32, i32, vp, i32, vp, i32, i32, vp, vp,
+                                                i32, vp]),
     "s1kv_batch_begin": (C.c_int, [vp, P(u64), P(i32), P(i32), i32, vp, P(vp)]),
     "s1kv_batch_sizes": (C.c_int, [vp, P(i64), P(i64)]),
     "s1kv_batch_rope_append": (C.c_int, [vp, i32, vp, vp, i32, vp, vp, vp]),
