@@ -66,7 +66,7 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
     if (!out || (n_seqs > 0 && !seqs) || n_seqs < 0) return set_error(S1KV_EINVAL, "s1kv_batch_begin: bad arguments");
     *out = nullptr;
     cudaStream_t stream = (cudaStream_t)stream_;
-    S1KV_CUDA(cudaSetDevice(p->device));
+    S1KV_ON_DEVICE(p->device);
     const int32_t bs = p->desc.block_size;
 
     auto* b = new s1kv_batch();
@@ -218,6 +218,7 @@ static int batch_append_impl(s1kv_batch* b, int32_t layer, const float* q_in, fl
     int st = check_layer(p, layer);
     if (st) return st;
     if (b->n_tokens == 0) return S1KV_OK;
+    S1KV_ON_DEVICE(p->device);
     if (!k || !v) return set_error(S1KV_EINVAL, "s1kv_batch_append: null k/v");
     if (q_in && (!q_out || Hq <= 0 || b->n_rows != b->n_tokens))
         return set_error(S1KV_EINVAL, "s1kv_batch_rope_append: q needs q_out, n_q_heads and one row per token");
@@ -260,6 +261,7 @@ int s1kv_batch_attention(s1kv_batch* b, int32_t layer, const float* q, float* ou
     s1kv_pool* p = b->pool;
     int st = check_layer(p, layer);
     if (st) return st;
+    S1KV_ON_DEVICE(p->device);
     const int32_t Hkv = p->desc.num_kv_heads, D = p->desc.head_dim;
     if (Hq <= 0 || Hq % Hkv) return set_error(S1KV_EINVAL, "s1kv_batch_attention: n_q_heads must be a multiple of num_kv_heads");
     if (b->n_rows == 0) return S1KV_OK;
@@ -301,6 +303,7 @@ int s1kv_batch_layer_host(s1kv_batch* b, int32_t layer, const float* h_q, const 
                           float* h_out, int32_t Hq, void* stream_) {
     if (!b) return set_error(S1KV_EINVAL, "null batch");
     s1kv_pool* p = b->pool;
+    S1KV_ON_DEVICE(p->device);
     cudaStream_t stream = (cudaStream_t)stream_;
     const int64_t D = p->desc.head_dim, Hkv = p->desc.num_kv_heads;
     const size_t qb = (size_t)b->n_rows * Hq * D * 4, kb = (size_t)b->n_tokens * Hkv * D * 4;
@@ -327,6 +330,7 @@ int s1kv_batch_layer_host(s1kv_batch* b, int32_t layer, const float* h_q, const 
 
 int s1kv_batch_end(s1kv_batch* b, void* stream) {
     if (!b) return S1KV_OK;
+    S1KV_ON_DEVICE(b->pool->device);
     int st = S1KV_OK;
     if (b->seg) st = b->pool->stager.release(b->seg, (cudaStream_t)stream);
     delete b;
@@ -340,7 +344,7 @@ int s1kv_append(s1kv_pool* p, int32_t layer, const float* k, const float* v, con
     int st = check_pool(p);
     if (!st) st = check_layer(p, layer);
     if (st) return st;
-    S1KV_CUDA(cudaSetDevice(p->device));
+    S1KV_ON_DEVICE(p->device);
     st = flush(p, (cudaStream_t)stream);
     if (st) return st;
     AppendParams ap{};
@@ -364,7 +368,7 @@ int s1kv_rope_append(s1kv_pool* p, int32_t layer, const float* q_in, float* q_ou
     if (!st) st = check_layer(p, layer);
     if (st) return st;
     if (q_in && (!q_out || Hq <= 0)) return set_error(S1KV_EINVAL, "s1kv_rope_append: q needs q_out and n_q_heads");
-    S1KV_CUDA(cudaSetDevice(p->device));
+    S1KV_ON_DEVICE(p->device);
     st = flush(p, (cudaStream_t)stream);
     if (st) return st;
     AppendParams ap{};
@@ -415,7 +419,7 @@ int s1kv_gather(s1kv_pool* p, int32_t layer, uint64_t seq, int32_t which, float*
     int64_t len;
     st = seq_row(p, seq, &row, &len);
     if (st) return st;
-    S1KV_CUDA(cudaSetDevice(p->device));
+    S1KV_ON_DEVICE(p->device);
     st = flush(p, (cudaStream_t)stream);
     if (st) return st;
     return launch_gather(p, layer, row, len, which, out, (cudaStream_t)stream);
@@ -424,7 +428,7 @@ int s1kv_gather(s1kv_pool* p, int32_t layer, uint64_t seq, int32_t which, float*
 int s1kv_cow_copy(s1kv_pool* p, const int32_t* src, const int32_t* dst, int64_t n, void* stream) {
     int st = check_pool(p);
     if (st) return st;
-    S1KV_CUDA(cudaSetDevice(p->device));
+    S1KV_ON_DEVICE(p->device);
     return launch_cow(p, src, dst, n, (cudaStream_t)stream);
 }
 
@@ -493,7 +497,7 @@ int s1kv_pool_read(s1kv_pool* p, int32_t layer, int32_t which, int64_t slot0, in
     if (st) return st;
     if (slot0 < 0 || n_slots < 0 || slot0 + n_slots > p->num_slots || (n_slots && !host_out))
         return set_error(S1KV_EINVAL, "s1kv_pool_read: slot range out of bounds");
-    S1KV_CUDA(cudaSetDevice(p->device));
+    S1KV_ON_DEVICE(p->device);
     S1KV_CUDA(cudaDeviceSynchronize());
     const size_t row = (size_t)p->desc.num_kv_heads * p->desc.head_dim * p->elem;
     const char* base = (which ? p->v : p->k) + (size_t)layer * p->layer_bytes + (size_t)slot0 * row;

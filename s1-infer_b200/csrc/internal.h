@@ -26,6 +26,30 @@ int cuda_error(cudaError_t e, const char* what);
 
 extern std::atomic<int64_t> g_launches;
 
+// Makes `device` current for the enclosing scope and restores the caller's
+// device on exit: entry points never change the calling thread's current
+// CUDA device (a process that drives one GPU per rank relies on it).
+struct DeviceGuard {
+    int prev = -1;
+    cudaError_t err = cudaSuccess;
+    explicit DeviceGuard(int device) {
+        int cur = 0;
+        err = cudaGetDevice(&cur);
+        if (err == cudaSuccess && cur != device) {
+            err = cudaSetDevice(device);
+            if (err == cudaSuccess) prev = cur;
+        }
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+};
+#define S1KV_ON_DEVICE(dev)                                            \
+    ::s1kv::DeviceGuard s1kv_device_guard_(dev);                       \
+    if (s1kv_device_guard_.err != cudaSuccess) return ::s1kv::cuda_error(s1kv_device_guard_.err, "cudaSetDevice")
+
 // Device error word bits (one word per device, shared by every kernel).
 constexpr int kErrBounds = 1;
 constexpr int kErrTimeout = 2;

@@ -422,7 +422,8 @@ int s1kv_pool_create(const s1kv_pool_desc* d, int device, s1kv_pool** out) {
     for (int32_t r = p->desc.max_seqs - 1; r >= 0; r--) p->free_rows.push_back(r);
 
     if (!p->host_only) {
-        cudaError_t e = cudaSetDevice(device);
+        DeviceGuard guard(device);
+        cudaError_t e = guard.err;
         size_t total = p->layer_bytes * d->num_layers;
         if (e == cudaSuccess) e = cudaMalloc((void**)&p->k, total);
         if (e == cudaSuccess) e = cudaMalloc((void**)&p->v, total);
@@ -460,6 +461,7 @@ int s1kv_pool_create(const s1kv_pool_desc* d, int device, s1kv_pool** out) {
 int s1kv_pool_destroy(s1kv_pool* p) {
     if (!p) return S1KV_OK;
     if (!p->host_only) {
+        DeviceGuard guard(p->device);
         cudaDeviceSynchronize();
         p->stager.destroy();
         p->scratch.destroy();
@@ -510,7 +512,7 @@ int s1kv_pool_check(s1kv_pool* p, int32_t* flags_out) {
 }
 
 int s1kv_device_check(int device, int32_t* flags_out) {
-    S1KV_CUDA(cudaSetDevice(device));
+    S1KV_ON_DEVICE(device);
     int* word = device_error_word(device);
     if (!word) return set_error(S1KV_ENOMEM, "s1kv: error word allocation failed");
     S1KV_CUDA(cudaDeviceSynchronize());
@@ -684,7 +686,7 @@ int s1kv_prefix_match(s1kv_pool* p, uint64_t dst, const int32_t* tokens, int64_t
 int s1kv_flush(s1kv_pool* p, void* stream) {
     if (!p) return set_error(S1KV_EINVAL, "null pool");
     if (p->host_only) return set_error(S1KV_EINVAL, "s1kv: host-only pool has no device storage");
-    S1KV_CUDA(cudaSetDevice(p->device));
+    S1KV_ON_DEVICE(p->device);
     return flush(p, (cudaStream_t)stream);
 }
 

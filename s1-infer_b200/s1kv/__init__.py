@@ -141,9 +141,11 @@ def _dptr(t):
 
 
 def _cuda_f32(x, device):
+    """float32 contiguous CUDA tensor on `device` (None = current device)."""
     import torch
     t = torch.as_tensor(x)
-    return t.to(device=device, dtype=torch.float32).contiguous()
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    return t.to(device=dev, dtype=torch.float32).contiguous()
 
 
 def launch_count():
@@ -163,9 +165,16 @@ class Pool:
     """A device-resident block pool of ``num_layers`` layers sharing one block
     table per sequence (include/s1kv.h)."""
 
-    def __init__(self, num_layers, num_kv_heads, head_dim, max_blocks, block_size=16, dtype="f32", device=0,
+    def __init__(self, num_layers, num_kv_heads, head_dim, max_blocks, block_size=16, dtype="f32", device=None,
                  max_seqs=1024, max_seq_len=0, rope_theta=1.0e6, initial_free_list=None, host_only=False):
+        """device None = torch's current CUDA device (0 for a host-only pool)."""
         self.L = lib()
+        if device is None:
+            if host_only:
+                device = 0
+            else:
+                import torch
+                device = torch.cuda.current_device()
         self.num_layers, self.Hkv, self.D = num_layers, num_kv_heads, head_dim
         self.max_blocks, self.bs = max_blocks, block_size
         self.dtype = DTYPE_F32 if dtype in ("f32", "fp32", "float32", DTYPE_F32) else DTYPE_BF16
@@ -394,7 +403,7 @@ class KVBlockPool:
     (include/infer/kv_block_pool.h:32), backed by a one-layer device pool.
     Tensors are [tokens, num_heads, head_dim] fp32 (numpy or torch)."""
 
-    def __init__(self, num_heads, head_dim, max_blocks, block_size=16, device=0, dtype="f32", initial_free_list=None):
+    def __init__(self, num_heads, head_dim, max_blocks, block_size=16, device=None, dtype="f32", initial_free_list=None):
         self.pool = Pool(1, num_heads, head_dim, max_blocks, block_size, dtype=dtype, device=device,
                          initial_free_list=initial_free_list)
         self.num_heads, self.head_dim, self.block_size = num_heads, head_dim, block_size
@@ -456,24 +465,24 @@ def gqa_attention_paged(Q, k_view, v_view, num_q_heads, num_kv_heads, head_dim):
     return pool.attention(0, [k_view.seq], [Q.shape[0]], Q.reshape(Q.shape[0], num_q_heads, head_dim), num_q_heads)
 
 
-def gqa_attention(Q, Kc, Vc, num_q_heads, num_kv_heads, head_dim, device=0):
+def gqa_attention(Q, Kc, Vc, num_q_heads, num_kv_heads, head_dim, device=None):
     """GQA_attention over contiguous K/V (include/nn/attention.h:8)."""
     import torch
     Q, Kc, Vc = _cuda_f32(Q, device), _cuda_f32(Kc, device), _cuda_f32(Vc, device)
-    out = torch.empty((Q.shape[0], num_q_heads, head_dim), dtype=torch.float32, device=device)
+    out = torch.empty((Q.shape[0], num_q_heads, head_dim), dtype=torch.float32, device=Q.device)
     check(lib().s1kv_attention_contig(_dptr(Q), _dptr(Kc), _dptr(Vc), Q.shape[0], Kc.shape[0], num_q_heads,
                                       num_kv_heads, head_dim, _dptr(out), _stream()))
     return out
 
 
-def apply_rope(x, start_pos=0, theta=1.0e6, device=0):
+def apply_rope(x, start_pos=0, theta=1.0e6, device=None):
     """apply_rope(input, start_pos) (include/nn/RoPE.h:4): [T, H, D] or [T, D]."""
     import torch
     x = _cuda_f32(x, device)
     shape = x.shape
     x3 = x.reshape(shape[0], -1, shape[-1])
     out = torch.empty_like(x3)
-    with torch.cuda.device(device):
+    with torch.cuda.device(x.device):
         check(lib().s1kv_apply_rope(_dptr(x3), _dptr(out), start_pos, x3.shape[0], x3.shape[1], x3.shape[2], theta,
                                     _stream()))
     return out.reshape(shape)
