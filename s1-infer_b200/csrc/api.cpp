@@ -169,6 +169,18 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
     b->n_rows = n_rows;
     b->n_items = (int64_t)items.size();
     b->n_part = n_part;
+    // Per-sequence view of the same rows, for the tensor-core prefill.
+    std::vector<PrefillSeq> pseqs(n_seqs);
+    {
+        int32_t q_start = 0;
+        for (int32_t i = 0; i < n_seqs; i++) {
+            const int32_t ql = q_lens ? q_lens[i] : (n_append ? n_append[i] : 0);
+            pseqs[i] = PrefillSeq{trow[i], (int32_t)lens[i], ql, q_start};
+            q_start += ql;
+            b->max_qlen = std::max(b->max_qlen, ql);
+        }
+    }
+    b->n_seqs = n_seqs;
 
     // Device block tables and pending copy-on-write copies first.
     st = flush(p, stream);
@@ -178,7 +190,8 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
     }
     // One upload of the step's metadata.
     size_t o_slots = 0, o_pos = align16(o_slots + n_tok * 4), o_rows = align16(o_pos + n_tok * 4),
-           o_items = align16(o_rows + n_rows * sizeof(RowMeta)), total = align16(o_items + items.size() * sizeof(WorkItem));
+           o_items = align16(o_rows + n_rows * sizeof(RowMeta)), o_pseq = align16(o_items + items.size() * sizeof(WorkItem)),
+           total = align16(o_pseq + pseqs.size() * sizeof(PrefillSeq));
     st = p->stager.acquire(total + 16, &b->seg);
     if (st) {
         delete b;
@@ -189,11 +202,13 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
     std::memcpy(h + o_pos, pos.data(), n_tok * 4);
     std::memcpy(h + o_rows, b->rows.data(), n_rows * sizeof(RowMeta));
     std::memcpy(h + o_items, items.data(), items.size() * sizeof(WorkItem));
+    std::memcpy(h + o_pseq, pseqs.data(), pseqs.size() * sizeof(PrefillSeq));
     if (total) S1KV_CUDA(cudaMemcpyAsync(b->seg->d, h, total, cudaMemcpyHostToDevice, stream));
     b->d_slots = (const int32_t*)(b->seg->d + o_slots);
     b->d_pos = (const int32_t*)(b->seg->d + o_pos);
     b->d_rows = (const RowMeta*)(b->seg->d + o_rows);
     b->d_items = (const WorkItem*)(b->seg->d + o_items);
+    b->d_pseqs = (const PrefillSeq*)(b->seg->d + o_pseq);
     *out = b;
     return S1KV_OK;
 }
@@ -268,6 +283,27 @@ int s1kv_batch_attention(s1kv_batch* b, int32_t layer, const float* q, float* ou
     if (!q || !out) return set_error(S1KV_EINVAL, "s1kv_batch_attention: null q/out");
     const int G = Hq / Hkv;
     cudaStream_t stream = (cudaStream_t)stream_;
+    // Chunks of several query rows per sequence over bf16 K/V are a dense
+    // contraction: tensor-core prefill.  Decode rows stay on the split-K
+    // kernel.
+    if (!b->decode_rows && p->tmap_sw_ok && prefill_tc_supported(p->desc.dtype, D, G, p->desc.block_size)) {
+        PrefillParams pp{};
+        pp.q = q;
+        pp.out = out;
+        pp.table = p->d_table;
+        pp.seqs = b->d_pseqs;
+        pp.n_seqs = b->n_seqs;
+        pp.max_chunks = (b->max_qlen + prefill_queries_per_cta(G) - 1) / prefill_queries_per_cta(G);
+        pp.max_bps = p->max_bps;
+        pp.max_blocks = (int32_t)p->desc.max_blocks;
+        pp.Hq = Hq;
+        pp.Hkv = Hkv;
+        pp.layer = layer;
+        pp.scale_log2 = scale_log2(D);
+        pp.err = p->d_err;
+        if (pp.n_seqs == 0 || pp.max_chunks == 0) return S1KV_OK;
+        return launch_prefill_tc(pp, p->tmap_k_sw, p->tmap_v_sw, stream);
+    }
     size_t need = (size_t)b->n_part * Hkv * G * (D + 2) * sizeof(float);
     if (need) {
         st = p->scratch.ensure(need);

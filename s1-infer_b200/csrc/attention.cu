@@ -667,6 +667,19 @@ int make_tensor_maps(s1kv_pool* p) {
         if (r != CUDA_SUCCESS) return set_error(S1KV_ECUDA, "s1kv: cuTensorMapEncodeTiled failed (%d)", (int)r);
     }
     p->tmap_ok = true;
+    // Tensor-core prefill reads 64-element halves of each row with 128B
+    // swizzle, the layout UMMA consumes (bf16 pools, head_dim 128).
+    p->tmap_sw_ok = false;
+    if (p->desc.dtype == S1KV_DTYPE_BF16 && D == 128) {
+        cuuint32_t box_sw[4] = {64, 1, 16, 1};
+        for (int which = 0; which < 2; which++) {
+            CUresult r = encode(which ? &p->tmap_v_sw : &p->tmap_k_sw, dt, 4, which ? (void*)p->v : (void*)p->k, dims,
+                                strides, box_sw, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) return set_error(S1KV_ECUDA, "s1kv: cuTensorMapEncodeTiled (swizzled) failed (%d)", (int)r);
+        }
+        p->tmap_sw_ok = true;
+    }
     return S1KV_OK;
 }
 

@@ -95,6 +95,29 @@ struct AttnParams {
     int* err;
 };
 
+// One sequence of a prefill batch (tensor-core prefill kernel).
+struct PrefillSeq {
+    int32_t table_row;
+    int32_t kv_len;
+    int32_t q_len;
+    int32_t q_start;  // first row of this sequence in q / out
+};
+
+struct PrefillParams {
+    const float* q;          // [rows][Hq][D] fp32, post-RoPE
+    float* out;
+    const int32_t* table;    // [max_seqs][max_bps]
+    const PrefillSeq* seqs;
+    int32_t n_seqs;
+    int32_t max_chunks;      // grid.x = n_seqs * max_chunks
+    int32_t max_bps;
+    int32_t max_blocks;
+    int32_t Hq, Hkv;
+    int32_t layer;
+    float scale_log2;
+    int* err;
+};
+
 struct AppendParams {
     const float* k;        // [n][Hkv][D]
     const float* v;
@@ -186,6 +209,9 @@ struct s1kv_pool {
     CUtensorMap tmap_k{};
     CUtensorMap tmap_v{};
     bool tmap_ok = false;
+    CUtensorMap tmap_k_sw{};  // 128B-swizzled 64-element boxes (tensor-core prefill)
+    CUtensorMap tmap_v_sw{};
+    bool tmap_sw_ok = false;
     // host bookkeeping
     std::vector<int32_t> free_list;   // LIFO, back() allocated first
     std::vector<int32_t> rc;
@@ -229,6 +255,9 @@ struct s1kv_batch {
     const int32_t* d_pos = nullptr;
     const s1kv::RowMeta* d_rows = nullptr;
     const s1kv::WorkItem* d_items = nullptr;
+    const s1kv::PrefillSeq* d_pseqs = nullptr;
+    int32_t n_seqs = 0;
+    int32_t max_qlen = 0;
     std::vector<s1kv::RowMeta> rows;  // host copy (for dispatch decisions)
 };
 
@@ -260,4 +289,9 @@ int encode_kv_maps(const void* k, const void* v, int dtype, int Hkv, int D, int6
                    CUtensorMap* tv);
 int launch_decode_with_maps(const AttnParams& p, const CUtensorMap& tk, const CUtensorMap& tv, int dtype,
                             cudaStream_t stream);
+
+// Tensor-core prefix-hit prefill (prefill_tc.cu).
+bool prefill_tc_supported(int dtype, int D, int G, int block_size);
+int prefill_queries_per_cta(int G);
+int launch_prefill_tc(const PrefillParams& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream);
 }  // namespace s1kv
