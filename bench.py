@@ -51,6 +51,15 @@ def load_peaks():
         return 6650.0, "fallback"
 
 
+def load_tflops_peak():
+    """Dense bf16 tensor peak for a kernel timed alone (the burst figure)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured bf16_tflops (burst, MEASURED_PEAKS.json)"
+    except Exception:
+        return 1590.0, "fallback 1590 TFLOP/s"
+
+
 def contexts(n_gpus):
     """Per-rank context lengths.  Weak scaling with identical per-GPU work:
     every rank serves its own 64 sequences drawn from U[128, 4096] with the
@@ -332,6 +341,81 @@ def cpu_reference_sample(ctx, n_threads, layers_sampled=1, repeats=2, seed=5):
     }
 
 
+def prefill_flops(prefix, suffixes, hq, d):
+    """QK^T + PV FLOPs of a causal prefix-hit prefill: 4*Hq*D per visible
+    (query, key) pair, query i of a suffix seeing prefix + i + 1 keys."""
+    return sum(4 * hq * d * (L * prefix + L * (L + 1) // 2) for L in suffixes)
+
+
+def run_cfg3(s1kv, torch, rank, reps=10):
+    """cfg3: 256 sequences fork one 2050-token prefix (128 full blocks plus
+    a 2-token tail, shared with refcounts); each appends a suffix of
+    U[64, 512] tokens (seed 2), which first copies the shared tail block
+    (copy-on-write), then runs the prefix-hit chunked prefill (tensor-core
+    kernel), then 32 decode steps.  bf16 K/V, Hq 32 / Hkv 8 / D 128, block
+    16; one layer (the workload names no layer count: figures are per
+    layer)."""
+    P, n, bs = 2050, 256, 16
+    rng = np.random.default_rng(2)
+    suff = [int(x) for x in rng.integers(64, 513, size=n)]
+    dec_steps = 32
+    blocks = (P + bs - 1) // bs + sum((L + dec_steps + bs) // bs + 1 for L in suff) + 8
+    order = rng.permutation(blocks).astype(np.int32)
+    pool = s1kv.Pool(1, HKV, D, blocks, bs, dtype="bf16", initial_free_list=order, max_seqs=n + 8)
+    gen = torch.Generator(device="cuda").manual_seed(23 + rank)
+    with pool.batch([0], [P], [0]) as b:
+        b.rope_append(0, torch.randn((P, HKV, D), device="cuda", generator=gen),
+                      torch.randn((P, HKV, D), device="cuda", generator=gen))
+    seqs = list(range(1, n + 1))
+    for s_ in seqs:
+        pool.fork(0, s_, P)
+    T = sum(suff)
+    q = torch.randn((T, HQ, D), device="cuda", generator=gen)
+    k = torch.randn((T, HKV, D), device="cuda", generator=gen)
+    v = torch.randn((T, HKV, D), device="cuda", generator=gen)
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    torch.cuda.synchronize()
+    e0.record()
+    with pool.batch(seqs, suff) as b:  # COW of every tail, RoPE+append, prefill
+        q_rot = b.rope_append(0, k, v, q=q)
+        e1.record()
+        out = b.attention(0, q_rot)
+        e2.record()
+        torch.cuda.synchronize()
+        step_ms = e0.elapsed_time(e2)
+        # the attention call is idempotent: time it alone, repeated
+        for _ in range(3):
+            b.attention(0, q_rot, out=out)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t0.record()
+        for _ in range(reps):
+            b.attention(0, q_rot, out=out)
+        t1.record()
+        torch.cuda.synchronize()
+    attn_ms = t0.elapsed_time(t1) / reps
+    flops = prefill_flops(P, suff, HQ, D)
+    cow = pool.stats()["cow_copies"]
+    # 32 decode steps of all 256 sequences (split-K decode over shared blocks)
+    qd = torch.randn((n, HQ, D), device="cuda", generator=gen)
+    kd = torch.randn((n, HKV, D), device="cuda", generator=gen)
+    vd = torch.randn((n, HKV, D), device="cuda", generator=gen)
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record()
+    for _ in range(dec_steps):
+        with pool.batch(seqs, [1] * n) as b:
+            qr = b.rope_append(0, kd, vd, q=qd)
+            b.attention(0, qr)
+    d1.record()
+    torch.cuda.synchronize()
+    dec_ms = d0.elapsed_time(d1) / dec_steps
+    assert pool.check_device() == 0
+    pool.close()
+    return {"prefill_attn_ms": attn_ms, "prefill_tflops": flops / (attn_ms * 1e-3) / 1e12, "prefill_flops": flops,
+            "prefill_step_ms": step_ms, "cow_copies": cow, "decode_ms_per_step": dec_ms,
+            "decode_tok_s_per_layer": n / (dec_ms * 1e-3)}
+
+
 def run_ours(args):
     import torch
     import s1kv
@@ -352,9 +436,12 @@ def run_ours(args):
             continue
         res[dtype] = run_variant(s1kv, torch, dtype, share, args.steps, args.warmup, rank, world,
                                  timed_e2e=not args.no_e2e, sample_clocks=(dtype == "f32"))
+    cfg3 = run_cfg3(s1kv, torch, rank) if not args.only or args.only == "cfg3" else None
     if args.only:
         # profiling case: one variant, no summary line
-        if rank == 0:
+        if rank == 0 and args.only == "cfg3":
+            print(json.dumps({"profiling_case": "cfg3", **cfg3}))
+        elif rank == 0:
             r = res[args.only]
             print(json.dumps({"profiling_case": args.only, "layers": LAYERS, "ms_per_step": r["elapsed_ms"] / args.steps,
                               "avg_launch_ms": r["avg_launch_ms"], "bytes_per_launch": r["bytes_per_launch"]}))
@@ -377,6 +464,7 @@ def run_ours(args):
     if rank != 0:
         return
     achieved = h["bytes_per_launch"] / (h["avg_launch_ms"] * 1e-3) / 1e9
+    tflops_peak, tflops_src = load_tflops_peak()
     bf_achieved = bf["bytes_per_launch"] / (bf["avg_launch_ms"] * 1e-3) / 1e9
     line = {
         "metric": METRIC,
@@ -414,7 +502,17 @@ def run_ours(args):
             "kv_gbs_per_gpu": bf["kv_bytes_step"] / (bf["elapsed_ms"] / args.steps * 1e-3) / 1e9,
             "roofline": {"achieved": bf_achieved, "peak": peak, "frac": bf_achieved / peak,
                          "avg_launch_ms": bf["avg_launch_ms"], "bytes_per_launch": bf["bytes_per_launch"]},
-            "e2e_tok_s": bf_tokens / (bf_e2e_ms * 1e-3)}},
+            "e2e_tok_s": bf_tokens / (bf_e2e_ms * 1e-3)},
+            "cfg3_prefix_prefill": None if cfg3 is None else {
+                "workload": "256 seqs fork a 2050-token prefix (COW of the 2-token tail), suffix U[64,512] seed 2, "
+                            "bf16, per layer",
+                "prefill_tflops": cfg3["prefill_tflops"], "unit": "TFLOP/s",
+                "roofline": {"bound": "tensor", "achieved": cfg3["prefill_tflops"], "peak": tflops_peak,
+                             "frac": cfg3["prefill_tflops"] / tflops_peak, "unit": "TFLOP/s",
+                             "peak_source": tflops_src},
+                "prefill_attn_ms_per_layer": cfg3["prefill_attn_ms"], "prefill_flops_per_layer": cfg3["prefill_flops"],
+                "prefill_step_ms_per_layer": cfg3["prefill_step_ms"], "cow_copies": cfg3["cow_copies"],
+                "decode_ms_per_step_per_layer": cfg3["decode_ms_per_step"]}},
         "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
     }
     print(json.dumps(line))
@@ -481,7 +579,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling cases only (the bench line uses 32)")
-    ap.add_argument("--only", choices=["f32", "bf16"], help="profiling case: run one storage variant")
+    ap.add_argument("--only", choices=["f32", "bf16", "cfg3"], help="profiling case: run one variant")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     globals()["LAYERS"] = args.layers

@@ -14,15 +14,19 @@
 //     by TMA (one 16-row x 64-element box per block and 128-byte half of a
 //     row, 128B swizzle, no multicast), double buffered, completion on
 //     mbarriers with bounded waits.
-//   * S = Q K^T (M 128, N 64, K 128) and O_tile = P V (M 128, N 128, K 64)
-//     are tcgen05.mma kind::f16 with fp32 accumulators in TMEM (S: 64
-//     columns, O_tile: 128 columns; 256 columns per CTA, 2 CTAs per SM).
-//     One thread issues; tcgen05.commit signals an mbarrier.
+//   * S = Q K^T (M 128, N 64, K 128) and O += P V (M 128, N 128, K 64) are
+//     tcgen05.mma kind::f16 with fp32 accumulators in TMEM: S double
+//     buffered (2 x 64 columns) so the scores of tile t+1 are computed while
+//     the threads run the softmax of tile t; O (128 columns) accumulates
+//     across all tiles.  256 columns per CTA, 2 CTAs per SM.  One thread
+//     issues; tcgen05.commit signals an mbarrier.
 //   * Each thread owns one accumulator row: it reads S with tcgen05.ld,
 //     applies the scale and the causal mask, runs the online softmax in the
-//     exp2 domain, writes P (bf16) in the swizzled K-major layout for the
-//     PV MMA into the current tile's K buffer (free once S is computed),
-//     then folds O_tile into its fp32 O row kept in registers.
+//     exp2 domain and writes P (bf16) in the swizzled K-major layout for the
+//     PV MMA into the current tile's K buffer (free once S is computed).
+//     The reference max only moves when the row max outgrows it by 2^8, and
+//     only then is the row of O in TMEM rescaled (tcgen05.ld/st), so the
+//     common tile does no per-row O work at all.
 // Every wait is bounded and decided for the whole CTA at once (a timeout
 // sets the device error word); copies in flight are drained and TMEM is
 // freed on every exit path.
@@ -42,8 +46,9 @@ constexpr int kM = 128;          // accumulator rows per CTA
 constexpr int kN = 64;           // tokens per K/V tile
 constexpr int kD = 128;          // head dim (two 64-element swizzle atoms)
 constexpr int kThreads = 128;    // one thread per accumulator row
-constexpr int kTmemCols = 256;   // S [0, 64), O_tile [128, 256)
+constexpr int kTmemCols = 256;   // S[0] [0, 64), S[1] [64, 128), O [128, 256)
 constexpr int kTmemS = 0, kTmemO = 128;
+constexpr float kRescaleAt = 8.0f;  // log2 units: O is rescaled only when a row max grows by > 2^8
 
 // shared memory layout (bytes, 1024-aligned pieces)
 constexpr int kQBytes = 2 * kM * 128;          // 2 atoms x 128 rows x 128 B = 32 KB
@@ -54,8 +59,10 @@ static_assert(kPBytes == kKBytes, "P reuses the tile's K buffer");
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kQBytes;         // K[2] (P of the tile aliases K[tile & 1])
 constexpr int kOffV = kOffK + 2 * kKBytes;     // V[2]
-constexpr int kOffBar = kOffV + 2 * kVBytes;   // kv[2], s, o mbarriers + tmem slot
-constexpr int kSmem = kOffBar + 64 + 1024;     // + slack for 1024 alignment of the base
+constexpr int kOffBar = kOffV + 2 * kVBytes;   // kv[2], s[2], o mbarriers + tmem slot
+constexpr int kIdsCached = 256;                // block ids of the first 64 tiles (4096 tokens)
+constexpr int kOffIds = kOffBar + 64;
+constexpr int kSmem = kOffIds + kIdsCached * 4 + 1024;  // + slack for 1024 alignment of the base
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -134,6 +141,23 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// Writes 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+        "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
+        "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ float ex2f(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -162,8 +186,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint8_t* sQ = smem + kOffQ;
     uint8_t* sK = smem + kOffK;
     uint8_t* sV = smem + kOffV;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);  // [0,1] kv, [2] s, [3] o
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + 32);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);  // [0,1] kv, [2,3] s, [4] o
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + 48);
 
     const int tid = threadIdx.x, warp = tid >> 5;
     const int seq_i = blockIdx.x / p.max_chunks, chunk = blockIdx.x % p.max_chunks;
@@ -190,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        for (int i = 0; i < 4; i++) bar_init(&bars[i], 1);
+        for (int i = 0; i < 5; i++) bar_init(&bars[i], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     // ---- Q: fp32 -> bf16, swizzled K-major ----
@@ -214,146 +238,200 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t tmem = *tmem_slot;
     const int32_t* tab = p.table + (int64_t)sm.table_row * p.max_bps;
 
-    auto issue_kv = [&](int t, int buf) {
+    // Block ids of the chunk's first kIdsCached blocks, looked up once.
+    // Blocks past the sequence end are not looked up: a box that starts out
+    // of range is zero-filled by TMA.
+    int32_t* sIds = reinterpret_cast<int32_t*>(smem + kOffIds);
+    auto lookup = [&](int i) -> int32_t {
+        if (i * 16 >= sm.kv_len) return p.max_blocks;
+        const int32_t blk = tab[i];
+        if ((uint32_t)blk >= (uint32_t)p.max_blocks) {
+            atomicOr(p.err, kErrBounds);
+            return p.max_blocks;
+        }
+        return blk;
+    };
+    for (int i = tid; i < min(n_tiles * (kN / 16), kIdsCached); i += kThreads) sIds[i] = lookup(i);
+    __syncthreads();
+
+    auto issue_kv = [&](int t) {
+        const int buf = t & 1;
         uint8_t* k = sK + buf * kKBytes;
         uint8_t* v = sV + buf * kVBytes;
         bar_expect(&bars[buf], kKBytes + kVBytes);
         for (int b = 0; b < kN / 16; b++) {
-            const int blk_i = t * (kN / 16) + b;
-            // Blocks past the sequence end are not looked up: a box that
-            // starts out of range is zero-filled by TMA.
-            int32_t blk = p.max_blocks;
-            if (blk_i * 16 < sm.kv_len) {
-                blk = tab[blk_i];
-                if ((uint32_t)blk >= (uint32_t)p.max_blocks) {
-                    atomicOr(p.err, kErrBounds);
-                    blk = p.max_blocks;
-                }
-            }
+            const int i = t * (kN / 16) + b;
+            const int32_t blk = i < kIdsCached ? sIds[i] : lookup(i);
             for (int a = 0; a < 2; a++) {
                 tma4(k + a * (kN * 128) + b * 16 * 128, &tmK, &bars[buf], a * 64, h, blk * 16, p.layer);
                 tma4(v + a * (kN * 128) + b * 16 * 128, &tmV, &bars[buf], a * 64, h, blk * 16, p.layer);
             }
         }
     };
-    if (tid == 0) issue_kv(0, 0);
-
     constexpr uint32_t idS = idesc_bf16(kM, kN, 0, 0);
     constexpr uint32_t idO = idesc_bf16(kM, kD, 0, 1);
-    float o[kD];
+    auto issue_s = [&](int t) {  // S[t&1] = Q K(t)^T
+        tc_fence_after();
+        const uint32_t qa = su32(sQ), ka = su32(sK + (t & 1) * kKBytes);
 #pragma unroll
-    for (int d = 0; d < kD; d++) o[d] = 0.0f;
-    float m = -INFINITY, l = 0.0f;
+        for (int ks = 0; ks < kD / 16; ks++) {
+            const uint32_t off = (ks & 3) * 32;  // 16 elements = 32 bytes inside the 128-byte atom row
+            const uint64_t da = sdesc(qa + (ks >> 2) * (kM * 128) + off, 16, 1024);
+            const uint64_t db = sdesc(ka + (ks >> 2) * (kN * 128) + off, 16, 1024);
+            mma_bf16(tmem + kTmemS + (t & 1) * kN, da, db, idS, ks > 0);
+        }
+        mma_commit(&bars[2 + (t & 1)]);
+    };
+    auto issue_pv = [&](int t) {  // O += P(t) V(t); P(t) lives in K(t)'s buffer
+        tc_fence_after();
+        const uint32_t pa = su32(sK + (t & 1) * kKBytes), va = su32(sV + (t & 1) * kVBytes);
+#pragma unroll
+        for (int ks = 0; ks < kN / 16; ks++) {
+            const uint64_t da = sdesc(pa + ks * 32, 16, 1024);
+            const uint64_t db = sdesc(va + ks * 16 * 128, kN * 128, 1024);
+            mma_bf16(tmem + kTmemO, da, db, idO, t > 0 || ks > 0);
+        }
+        mma_commit(&bars[4]);
+    };
+
+    // Issue schedule (thread 0): S(t+1) runs on the tensor core while the
+    // threads do the softmax of tile t; PV(t) follows; K/V buffer t&1 is
+    // refilled with tile t+2 once PV(t) has read P(t) and V(t).
+    int kv_issued = 0, kv_waited = 0, s_issued = 0, pv_issued = 0, pv_waited = 0;
+    bool issue_ok = true;
+    if (tid == 0) {
+        issue_kv(0);
+        kv_issued = 1;
+        if (n_tiles > 1) issue_kv(1), kv_issued = 2;
+        issue_ok = bar_wait(&bars[0], 0);
+        kv_waited = 1;
+        if (issue_ok) issue_s(0), s_issued = 1;
+        if (issue_ok && n_tiles > 1) {
+            issue_ok = bar_wait(&bars[1], 0);
+            kv_waited = 2;
+            if (issue_ok) issue_s(1), s_issued = 2;
+        }
+    }
+
+    float m = -INFINITY;  // running max actually used for p (lags the true max by < 2^8)
+    float l = 0.0f;
     bool ok = true;
-    // What is in flight, for the drain on the error path: the K/V copy of
-    // the next tile (barrier, parity) and the last committed MMA group.
-    int kv_bar = 0, kv_par = 0;   // tile 0 is issued below
-    int mma_bar = -1, mma_par = 0;
+    int s_waited = 0;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
 
     for (int t = 0; t < n_tiles; t++) {
-        const int buf = t & 1;
-        uint8_t* sP = sK + buf * kKBytes;  // P of this tile: K[buf] is free once S is done
-        if (!__syncthreads_and(bar_wait(&bars[buf], (uint32_t)((t >> 1) & 1)))) {
+        // 1. scores of tile t (PV(t-1) is complete too: thread 0 waited for it
+        //    before arriving here)
+        if (!__syncthreads_and(bar_wait(&bars[2 + (t & 1)], (uint32_t)((t >> 1) & 1)))) {
             ok = false;
             break;
         }
-        kv_bar = -1;
-        if (tid == 0) {
-            if (t + 1 < n_tiles) issue_kv(t + 1, buf ^ 1);
-            tc_fence_after();
-            const uint32_t qa = su32(sQ), ka = su32(sK + buf * kKBytes);
-#pragma unroll
-            for (int ks = 0; ks < kD / 16; ks++) {
-                const uint32_t off = (ks & 3) * 32;  // 16 elements = 32 bytes inside the 128-byte atom row
-                const uint64_t da = sdesc(qa + (ks >> 2) * (kM * 128) + off, 16, 1024);
-                const uint64_t db = sdesc(ka + (ks >> 2) * (kN * 128) + off, 16, 1024);
-                mma_bf16(tmem + kTmemS, da, db, idS, ks > 0);
-            }
-            mma_commit(&bars[2]);
-        }
-        if (t + 1 < n_tiles) kv_bar = buf ^ 1, kv_par = ((t + 1) >> 1) & 1;
-        mma_bar = 2, mma_par = t & 1;
-        if (!__syncthreads_and(bar_wait(&bars[2], (uint32_t)(t & 1)))) {
-            ok = false;
-            break;
-        }
-        mma_bar = -1;
+        s_waited = t + 1;
         tc_fence_after();
-        // ---- softmax on this row's 64 scores ----
-        float s[kN];
-        tmem_ld32(tmem + lane_base + kTmemS, s);
-        tmem_ld32(tmem + lane_base + kTmemS + 32, s + 32);
+        // 2. online softmax of this row
+        float sc[kN];
+        tmem_ld32(tmem + lane_base + kTmemS + (t & 1) * kN, sc);
+        tmem_ld32(tmem + lane_base + kTmemS + (t & 1) * kN + 32, sc + 32);
         const int base = t * kN;
         float mx = -INFINITY;
+        if (base + kN - 1 <= prefix + q0) {  // whole tile visible to every row of the chunk
 #pragma unroll
-        for (int j = 0; j < kN; j++) {
-            s[j] = (base + j <= row_limit) ? s[j] * p.scale_log2 : -INFINITY;
-            mx = fmaxf(mx, s[j]);
+            for (int j = 0; j < kN; j++) {
+                sc[j] *= p.scale_log2;
+                mx = fmaxf(mx, sc[j]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < kN; j++) {
+                sc[j] = (base + j <= row_limit) ? sc[j] * p.scale_log2 : -INFINITY;
+                mx = fmaxf(mx, sc[j]);
+            }
         }
-        const float mn = fmaxf(m, mx);
-        const float mref = mn == -INFINITY ? 0.0f : mn;  // a fully masked row keeps p = 0
-        const float corr = ex2f(m - mref);
-        m = mn;
+        // Raise the reference max only when the row max outgrows it by more
+        // than 2^8; then O (in TMEM, complete up to tile t-1) and l are
+        // rescaled.  Otherwise p = 2^(s - m) <= 2^8 stays well inside fp32
+        // and bf16 range and the final O / l is unchanged.
+        const bool raise = mx > m + kRescaleAt;
+        float corr = 1.0f;
+        if (raise) {
+            corr = ex2f(m - mx);  // 0 on the first tile (m = -inf)
+            m = mx;
+            l *= corr;
+        }
+        if (t > 0 && __any_sync(0xffffffffu, raise)) {
+#pragma unroll
+            for (int c = 0; c < kD / 32; c++) {
+                float ov[32];
+                tmem_ld32(tmem + lane_base + kTmemO + c * 32, ov);
+#pragma unroll
+                for (int j = 0; j < 32; j++) ov[j] *= corr;
+                tmem_st32(tmem + lane_base + kTmemO + c * 32, ov);
+            }
+        }
+        const float mref = m == -INFINITY ? 0.0f : m;  // a row with nothing visible yet keeps p = 0
         float ls = 0.0f;
+        uint8_t* sP = sK + (t & 1) * kKBytes;
 #pragma unroll
         for (int c = 0; c < 8; c++) {
             float pv[8];
 #pragma unroll
             for (int e = 0; e < 8; e++) {
-                pv[e] = ex2f(s[c * 8 + e] - mref);
+                pv[e] = ex2f(sc[c * 8 + e] - mref);
                 ls += pv[e];
             }
             uint4 w = make_uint4(pack_bf16(pv[0], pv[1]), pack_bf16(pv[2], pv[3]), pack_bf16(pv[4], pv[5]),
                                  pack_bf16(pv[6], pv[7]));
             *reinterpret_cast<uint4*>(sP + swz(r, c)) = w;
         }
-        l = l * corr + ls;
+        l += ls;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         tc_fence_before();
         __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t pa = su32(sP), va = su32(sV + buf * kVBytes);
-#pragma unroll
-            for (int ks = 0; ks < kN / 16; ks++) {
-                const uint64_t da = sdesc(pa + ks * 32, 16, 1024);
-                const uint64_t db = sdesc(va + ks * 16 * 128, kN * 128, 1024);
-                mma_bf16(tmem + kTmemO, da, db, idO, ks > 0);
+        // 3. issue PV(t); then, once K(t+2)'s buffer is free, the next copy
+        //    and the scores two tiles ahead
+        if (tid == 0 && issue_ok) {
+            issue_pv(t);
+            pv_issued = t + 1;
+            issue_ok = bar_wait(&bars[4], (uint32_t)(t & 1));
+            pv_waited = t + 1;
+            if (issue_ok && t + 2 < n_tiles) {
+                issue_kv(t + 2);
+                kv_issued = t + 3;
+                issue_ok = bar_wait(&bars[(t + 2) & 1], (uint32_t)(((t + 2) >> 1) & 1));
+                kv_waited = t + 3;
+                if (issue_ok) issue_s(t + 2), s_issued = t + 3;
             }
-            mma_commit(&bars[3]);
         }
-        mma_bar = 3, mma_par = t & 1;
-        if (!__syncthreads_and(bar_wait(&bars[3], (uint32_t)(t & 1)))) {
-            ok = false;
-            break;
-        }
-        mma_bar = -1;
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < kD / 32; c++) {
-            float ot[32];
-            tmem_ld32(tmem + lane_base + kTmemO + c * 32, ot);
-#pragma unroll
-            for (int j = 0; j < 32; j++) o[c * 32 + j] = fmaf(o[c * 32 + j], corr, ot[j]);
-        }
-        tc_fence_before();
-        __syncthreads();
     }
 
-    if (!ok) {
+    if (ok) {
+        // the last PV was waited for by thread 0; make it visible to all
+        ok = __syncthreads_and(issue_ok || tid != 0);
+    } else if (tid == 0) {
         // Drain what is still in flight (bounded again) before TMEM and
         // shared memory are released.
-        if (tid == 0) atomicOr(p.err, kErrTimeout);
-        if (mma_bar >= 0) bar_wait(&bars[mma_bar], (uint32_t)mma_par);
-        if (kv_bar >= 0) bar_wait(&bars[kv_bar], (uint32_t)kv_par);
+        atomicOr(p.err, kErrTimeout);
+        for (int i = s_waited; i < s_issued; i++) bar_wait(&bars[2 + (i & 1)], (uint32_t)((i >> 1) & 1));
+        for (int i = pv_waited; i < pv_issued; i++) bar_wait(&bars[4], (uint32_t)(i & 1));
+        for (int i = kv_waited; i < kv_issued; i++) bar_wait(&bars[i & 1], (uint32_t)((i >> 1) & 1));
     }
-    if (ok && row_valid) {
+    if (ok) {
+        tc_fence_after();
         const float inv = 1.0f / l;
         float* orow = p.out + ((int64_t)(sm.q_start + q0 + qi) * p.Hq + h * G + g) * kD;
 #pragma unroll
-        for (int d = 0; d < kD; d += 4)
-            *reinterpret_cast<float4*>(orow + d) = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+        for (int c = 0; c < kD / 32; c++) {
+            float ov[32];
+            tmem_ld32(tmem + lane_base + kTmemO + c * 32, ov);
+            if (row_valid) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(orow + c * 32 + j) =
+                        make_float4(ov[j] * inv, ov[j + 1] * inv, ov[j + 2] * inv, ov[j + 3] * inv);
+            }
+        }
+    } else if (tid == 0) {
+        atomicOr(p.err, kErrTimeout);
     }
     // ---- tear-down: every path frees TMEM ----
     tc_fence_before();
