@@ -42,26 +42,30 @@ namespace s1kv {
 namespace {
 
 constexpr uint32_t kSpin = 1u << 22;
-constexpr int kM = 128;          // accumulator rows per CTA
+constexpr int kM = 128;          // accumulator rows per query tile (= TMEM lanes)
 constexpr int kN = 64;           // tokens per K/V tile
 constexpr int kD = 128;          // head dim (two 64-element swizzle atoms)
-constexpr int kThreads = 128;    // one thread per accumulator row
-constexpr int kTmemCols = 256;   // S[0] [0, 64), S[1] [64, 128), O [128, 256)
-constexpr int kTmemS = 0, kTmemO = 128;
+constexpr int kR = 3;            // K/V ring depth
+constexpr int kSoftmaxThreads = 256;  // two warpgroups, one per query tile
+constexpr int kThreads = kSoftmaxThreads + 64;  // + TMA warp + MMA warp
+constexpr int kTmemCols = 512;   // S_A [0,64), S_B [64,128), O_A [128,256), O_B [256,384)
 constexpr float kRescaleAt = 8.0f;  // log2 units: O is rescaled only when a row max grows by > 2^8
 
 // shared memory layout (bytes, 1024-aligned pieces)
-constexpr int kQBytes = 2 * kM * 128;          // 2 atoms x 128 rows x 128 B = 32 KB
-constexpr int kKBytes = 2 * kN * 128;          // 2 atoms x 64 rows x 128 B  = 16 KB
+constexpr int kQBytes = 2 * kM * 128;          // one query tile: 2 atoms x 128 rows x 128 B = 32 KB
+constexpr int kPBytes = kM * 128;              // P of one query tile: 64 tokens x 128 rows = 16 KB
+constexpr int kKBytes = 2 * kN * 128;          // 2 atoms x 64 rows x 128 B = 16 KB
 constexpr int kVBytes = 2 * kN * 128;          // 2 d-atoms x 64 tokens x 128 B = 16 KB
-constexpr int kPBytes = kM * 128;              // 1 atom (64 tokens) x 128 rows x 128 B = 16 KB, in K[buf]
-static_assert(kPBytes == kKBytes, "P reuses the tile's K buffer");
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kQBytes;         // K[2] (P of the tile aliases K[tile & 1])
-constexpr int kOffV = kOffK + 2 * kKBytes;     // V[2]
-constexpr int kOffBar = kOffV + 2 * kVBytes;   // kv[2], s[2], o mbarriers + tmem slot
-constexpr int kIdsCached = 256;                // block ids of the first 64 tiles (4096 tokens)
-constexpr int kOffIds = kOffBar + 64;
+constexpr int kOffQ = 0;                        // Q_A, Q_B
+constexpr int kOffP = kOffQ + 2 * kQBytes;      // P_A, P_B
+constexpr int kOffK = kOffP + 2 * kPBytes;      // K ring
+constexpr int kOffV = kOffK + kR * kKBytes;     // V ring
+constexpr int kOffBar = kOffV + kR * kVBytes;
+// barriers: k_full[R], k_empty[R], v_full[R], v_empty[R], s_full[2], p_full[2], pv_done[2], drain
+constexpr int kNumBars = 4 * kR + 7;
+constexpr int kOffMisc = kOffBar + kNumBars * 8;  // tmem slot, abort flag
+constexpr int kIdsCached = 256;                   // block ids of the first 64 tiles (4096 tokens)
+constexpr int kOffIds = (kOffMisc + 16 + 15) / 16 * 16;
 constexpr int kSmem = kOffIds + kIdsCached * 4 + 1024;  // + slack for 1024 alignment of the base
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -173,40 +177,57 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 // atom whose rows are 128 bytes: the chunk index is XORed with r mod 8.
 __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
+
+// Bounded wait that also gives up when another role of the CTA raised the
+// abort flag; a timeout raises it.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* b, uint32_t phase, volatile int* abort_flag) {
+    for (uint32_t i = 0; i < kSpin; i++) {
+        if (bar_try(b, phase)) return true;
+        if (*abort_flag) return false;
+    }
+    *abort_flag = 1;
+    return false;
+}
+
+__device__ __forceinline__ void bar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+
 }  // namespace
 
-// Queries per CTA: 128 rows / G heads.
+// Queries per query tile: 128 rows / G heads; a CTA takes two tiles.
 template <int G>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV) {
     constexpr int QT = kM / G;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t* sQ = smem + kOffQ;
-    uint8_t* sK = smem + kOffK;
-    uint8_t* sV = smem + kOffV;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);  // [0,1] kv, [2,3] s, [4] o
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + 48);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint64_t* k_full = bars;
+    uint64_t* k_empty = bars + kR;
+    uint64_t* v_full = bars + 2 * kR;
+    uint64_t* v_empty = bars + 3 * kR;
+    uint64_t* s_full = bars + 4 * kR;       // [2]
+    uint64_t* p_full = bars + 4 * kR + 2;   // [2]
+    uint64_t* pv_done = bars + 4 * kR + 4;  // [2]
+    uint64_t* drain = bars + 4 * kR + 6;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
+    int32_t* sIds = reinterpret_cast<int32_t*>(smem + kOffIds);
 
     const int tid = threadIdx.x, warp = tid >> 5;
     const int seq_i = blockIdx.x / p.max_chunks, chunk = blockIdx.x % p.max_chunks;
     const int h = blockIdx.y;
     const PrefillSeq sm = p.seqs[seq_i];
-    const int q0 = chunk * QT;
+    const int q0 = chunk * 2 * QT;
     if (q0 >= sm.q_len) return;  // uniform: no TMEM allocated yet
     const int prefix = sm.kv_len - sm.q_len;
-    // tokens the last query of the chunk may see
-    const int kv_end = min(sm.kv_len, prefix + q0 + QT);
+    const int kv_end = min(sm.kv_len, prefix + q0 + 2 * QT);  // tokens the last query may see
     const int n_tiles = (kv_end + kN - 1) / kN;
+    const int32_t* tab = p.table + (int64_t)sm.table_row * p.max_bps;
 
-    // This thread's accumulator row: head g, query i of the chunk.
-    const int r = tid;
-    const int g = r / QT, qi = r % QT;
-    const bool row_valid = q0 + qi < sm.q_len;
-    const int row_limit = prefix + q0 + qi;  // last visible token
-
-    // ---- set-up: TMEM, barriers ----
+    // ---- set-up ----
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
                      "r"(kTmemCols)
@@ -214,16 +235,33 @@ __global__ void __launch_bounds__(kThreads, 2)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        for (int i = 0; i < 5; i++) bar_init(&bars[i], 1);
+        for (int i = 0; i < kNumBars; i++) bar_init(&bars[i], 1);
+        bar_init(&p_full[0], 128);
+        bar_init(&p_full[1], 128);
+        *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    // ---- Q: fp32 -> bf16, swizzled K-major ----
-    {
-        const float* qrow = p.q + ((int64_t)(sm.q_start + min(q0 + qi, sm.q_len - 1)) * p.Hq + h * G + g) * kD;
+    auto lookup = [&](int i) -> int32_t {
+        if (i * 16 >= sm.kv_len) return p.max_blocks;  // past the end: zero-filled box
+        const int32_t blk = tab[i];
+        if ((uint32_t)blk >= (uint32_t)p.max_blocks) {
+            atomicOr(p.err, kErrBounds);
+            return p.max_blocks;
+        }
+        return blk;
+    };
+    for (int i = tid; i < min(n_tiles * (kN / 16), kIdsCached); i += kThreads) sIds[i] = lookup(i);
+    // Q tiles (softmax threads): row r of tile X is head r / QT, query X*QT + r % QT.
+    if (tid < kSoftmaxThreads) {
+        const int X = tid >> 7, r = tid & 127;
+        const int g = r / QT, qi = X * QT + r % QT;
+        const bool valid = q0 + qi < sm.q_len;
+        const float* qrow = p.q + ((int64_t)(sm.q_start + (valid ? q0 + qi : 0)) * p.Hq + h * G + g) * kD;
+        uint8_t* sQ = smem + kOffQ + X * kQBytes;
 #pragma unroll 4
-        for (int c = 0; c < 16; c++) {  // 16 chunks of 8 elements
+        for (int c = 0; c < 16; c++) {
             float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-            if (row_valid) {
+            if (valid) {
                 a = __ldg(reinterpret_cast<const float4*>(qrow + c * 8));
                 b = __ldg(reinterpret_cast<const float4*>(qrow + c * 8 + 4));
             }
@@ -236,206 +274,199 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int32_t* tab = p.table + (int64_t)sm.table_row * p.max_bps;
 
-    // Block ids of the chunk's first kIdsCached blocks, looked up once.
-    // Blocks past the sequence end are not looked up: a box that starts out
-    // of range is zero-filled by TMA.
-    int32_t* sIds = reinterpret_cast<int32_t*>(smem + kOffIds);
-    auto lookup = [&](int i) -> int32_t {
-        if (i * 16 >= sm.kv_len) return p.max_blocks;
-        const int32_t blk = tab[i];
-        if ((uint32_t)blk >= (uint32_t)p.max_blocks) {
-            atomicOr(p.err, kErrBounds);
-            return p.max_blocks;
-        }
-        return blk;
-    };
-    for (int i = tid; i < min(n_tiles * (kN / 16), kIdsCached); i += kThreads) sIds[i] = lookup(i);
-    __syncthreads();
-
-    auto issue_kv = [&](int t) {
-        const int buf = t & 1;
-        uint8_t* k = sK + buf * kKBytes;
-        uint8_t* v = sV + buf * kVBytes;
-        bar_expect(&bars[buf], kKBytes + kVBytes);
-        for (int b = 0; b < kN / 16; b++) {
-            const int i = t * (kN / 16) + b;
-            const int32_t blk = i < kIdsCached ? sIds[i] : lookup(i);
-            for (int a = 0; a < 2; a++) {
-                tma4(k + a * (kN * 128) + b * 16 * 128, &tmK, &bars[buf], a * 64, h, blk * 16, p.layer);
-                tma4(v + a * (kN * 128) + b * 16 * 128, &tmV, &bars[buf], a * 64, h, blk * 16, p.layer);
+    if (warp == kSoftmaxThreads / 32) {
+        // ================= TMA producer: K/V ring, runs ahead =================
+        if ((tid & 31) == 0) {
+            for (int t = 0; t < n_tiles; t++) {
+                const int slot = t % kR, use = t / kR;
+                if (t >= kR && !wait_or_abort(&k_empty[slot], (uint32_t)((use - 1) & 1), abort_flag)) break;
+                uint8_t* kb = smem + kOffK + slot * kKBytes;
+                bar_expect(&k_full[slot], kKBytes);
+                for (int b = 0; b < kN / 16; b++) {
+                    const int i = t * (kN / 16) + b;
+                    const int32_t blk = i < kIdsCached ? sIds[i] : lookup(i);
+                    for (int a = 0; a < 2; a++)
+                        tma4(kb + a * (kN * 128) + b * 16 * 128, &tmK, &k_full[slot], a * 64, h, blk * 16, p.layer);
+                }
+                if (t >= kR && !wait_or_abort(&v_empty[slot], (uint32_t)((use - 1) & 1), abort_flag)) {
+                    // K(t) is in flight; drain it before leaving
+                    wait_or_abort(&k_full[slot], (uint32_t)(use & 1), abort_flag);
+                    break;
+                }
+                uint8_t* vb = smem + kOffV + slot * kVBytes;
+                bar_expect(&v_full[slot], kVBytes);
+                for (int b = 0; b < kN / 16; b++) {
+                    const int i = t * (kN / 16) + b;
+                    const int32_t blk = i < kIdsCached ? sIds[i] : lookup(i);
+                    for (int a = 0; a < 2; a++)
+                        tma4(vb + a * (kN * 128) + b * 16 * 128, &tmV, &v_full[slot], a * 64, h, blk * 16, p.layer);
+                }
             }
         }
-    };
-    constexpr uint32_t idS = idesc_bf16(kM, kN, 0, 0);
-    constexpr uint32_t idO = idesc_bf16(kM, kD, 0, 1);
-    auto issue_s = [&](int t) {  // S[t&1] = Q K(t)^T
-        tc_fence_after();
-        const uint32_t qa = su32(sQ), ka = su32(sK + (t & 1) * kKBytes);
+    } else if (warp == kSoftmaxThreads / 32 + 1) {
+        // ================= MMA issuer =================
+        if ((tid & 31) == 0) {
+            constexpr uint32_t idS = idesc_bf16(kM, kN, 0, 0);
+            constexpr uint32_t idO = idesc_bf16(kM, kD, 0, 1);
+            const uint32_t qa[2] = {su32(smem + kOffQ), su32(smem + kOffQ + kQBytes)};
+            const uint32_t pa[2] = {su32(smem + kOffP), su32(smem + kOffP + kPBytes)};
+            auto issue_s = [&](int X, int t) {
+                const uint32_t ka = su32(smem + kOffK + (t % kR) * kKBytes);
 #pragma unroll
-        for (int ks = 0; ks < kD / 16; ks++) {
-            const uint32_t off = (ks & 3) * 32;  // 16 elements = 32 bytes inside the 128-byte atom row
-            const uint64_t da = sdesc(qa + (ks >> 2) * (kM * 128) + off, 16, 1024);
-            const uint64_t db = sdesc(ka + (ks >> 2) * (kN * 128) + off, 16, 1024);
-            mma_bf16(tmem + kTmemS + (t & 1) * kN, da, db, idS, ks > 0);
-        }
-        mma_commit(&bars[2 + (t & 1)]);
-    };
-    auto issue_pv = [&](int t) {  // O += P(t) V(t); P(t) lives in K(t)'s buffer
-        tc_fence_after();
-        const uint32_t pa = su32(sK + (t & 1) * kKBytes), va = su32(sV + (t & 1) * kVBytes);
+                for (int ks = 0; ks < kD / 16; ks++) {
+                    const uint32_t off = (ks & 3) * 32;  // 16 elements = 32 bytes inside a 128-byte atom row
+                    const uint64_t da = sdesc(qa[X] + (ks >> 2) * (kM * 128) + off, 16, 1024);
+                    const uint64_t db = sdesc(ka + (ks >> 2) * (kN * 128) + off, 16, 1024);
+                    mma_bf16(tmem + X * kN, da, db, idS, ks > 0);
+                }
+                mma_commit(&s_full[X]);
+            };
+            auto issue_pv = [&](int X, int t) {
+                const uint32_t va = su32(smem + kOffV + (t % kR) * kVBytes);
 #pragma unroll
-        for (int ks = 0; ks < kN / 16; ks++) {
-            const uint64_t da = sdesc(pa + ks * 32, 16, 1024);
-            const uint64_t db = sdesc(va + ks * 16 * 128, kN * 128, 1024);
-            mma_bf16(tmem + kTmemO, da, db, idO, t > 0 || ks > 0);
-        }
-        mma_commit(&bars[4]);
-    };
-
-    // Issue schedule (thread 0): S(t+1) runs on the tensor core while the
-    // threads do the softmax of tile t; PV(t) follows; K/V buffer t&1 is
-    // refilled with tile t+2 once PV(t) has read P(t) and V(t).
-    int kv_issued = 0, kv_waited = 0, s_issued = 0, pv_issued = 0, pv_waited = 0;
-    bool issue_ok = true;
-    if (tid == 0) {
-        issue_kv(0);
-        kv_issued = 1;
-        if (n_tiles > 1) issue_kv(1), kv_issued = 2;
-        issue_ok = bar_wait(&bars[0], 0);
-        kv_waited = 1;
-        if (issue_ok) issue_s(0), s_issued = 1;
-        if (issue_ok && n_tiles > 1) {
-            issue_ok = bar_wait(&bars[1], 0);
-            kv_waited = 2;
-            if (issue_ok) issue_s(1), s_issued = 2;
-        }
-    }
-
-    float m = -INFINITY;  // running max actually used for p (lags the true max by < 2^8)
-    float l = 0.0f;
-    bool ok = true;
-    int s_waited = 0;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-
-    for (int t = 0; t < n_tiles; t++) {
-        // 1. scores of tile t (PV(t-1) is complete too: thread 0 waited for it
-        //    before arriving here)
-        if (!__syncthreads_and(bar_wait(&bars[2 + (t & 1)], (uint32_t)((t >> 1) & 1)))) {
-            ok = false;
-            break;
-        }
-        s_waited = t + 1;
-        tc_fence_after();
-        // 2. online softmax of this row
-        float sc[kN];
-        tmem_ld32(tmem + lane_base + kTmemS + (t & 1) * kN, sc);
-        tmem_ld32(tmem + lane_base + kTmemS + (t & 1) * kN + 32, sc + 32);
-        const int base = t * kN;
-        float mx = -INFINITY;
-        if (base + kN - 1 <= prefix + q0) {  // whole tile visible to every row of the chunk
-#pragma unroll
-            for (int j = 0; j < kN; j++) {
-                sc[j] *= p.scale_log2;
-                mx = fmaxf(mx, sc[j]);
+                for (int ks = 0; ks < kN / 16; ks++) {
+                    const uint64_t da = sdesc(pa[X] + ks * 32, 16, 1024);
+                    const uint64_t db = sdesc(va + ks * 16 * 128, kN * 128, 1024);
+                    mma_bf16(tmem + 128 + X * 128, da, db, idO, t > 0 || ks > 0);
+                }
+                mma_commit(&pv_done[X]);
+            };
+            // Tensor-core order: S_A0 S_B0 | PV_A0 S_A1 PV_B0 S_B1 | PV_A1 S_A2 ...
+            // so one warpgroup's softmax always overlaps the other's MMAs.
+            bool ok = wait_or_abort(&k_full[0], 0, abort_flag);
+            if (ok) {
+                tc_fence_after();
+                issue_s(0, 0);
+                issue_s(1, 0);
+                mma_commit(&k_empty[0]);
             }
-        } else {
-#pragma unroll
-            for (int j = 0; j < kN; j++) {
-                sc[j] = (base + j <= row_limit) ? sc[j] * p.scale_log2 : -INFINITY;
-                mx = fmaxf(mx, sc[j]);
+            for (int t = 0; t < n_tiles && ok; t++) {
+                const int slot = t % kR;
+                ok = wait_or_abort(&p_full[0], (uint32_t)(t & 1), abort_flag) &&
+                     wait_or_abort(&v_full[slot], (uint32_t)((t / kR) & 1), abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv(0, t);
+                const bool more = t + 1 < n_tiles;
+                const int ns = (t + 1) % kR;
+                if (more) {
+                    ok = wait_or_abort(&k_full[ns], (uint32_t)(((t + 1) / kR) & 1), abort_flag);
+                    if (!ok) break;
+                    issue_s(0, t + 1);
+                }
+                ok = wait_or_abort(&p_full[1], (uint32_t)(t & 1), abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv(1, t);
+                mma_commit(&v_empty[slot]);
+                if (more) {
+                    issue_s(1, t + 1);
+                    mma_commit(&k_empty[ns]);
+                }
             }
+            // everything this thread issued has finished before TMEM is freed
+            mma_commit(drain);
+            bar_wait(drain, 0);
         }
-        // Raise the reference max only when the row max outgrows it by more
-        // than 2^8; then O (in TMEM, complete up to tile t-1) and l are
-        // rescaled.  Otherwise p = 2^(s - m) <= 2^8 stays well inside fp32
-        // and bf16 range and the final O / l is unchanged.
-        const bool raise = mx > m + kRescaleAt;
-        float corr = 1.0f;
-        if (raise) {
-            corr = ex2f(m - mx);  // 0 on the first tile (m = -inf)
-            m = mx;
-            l *= corr;
+    } else {
+        // ================= softmax warpgroups =================
+        const int X = tid >> 7, r = tid & 127;
+        const int g = r / QT, qi = X * QT + r % QT;
+        const bool valid = q0 + qi < sm.q_len;
+        const int row_limit = prefix + q0 + qi;  // last visible token
+        const uint32_t lane_base = (uint32_t)(32 * ((tid >> 5) & 3)) << 16;
+        const uint32_t tS = tmem + lane_base + X * kN;
+        const uint32_t tO = tmem + lane_base + 128 + X * 128;
+        uint8_t* sP = smem + kOffP + X * kPBytes;
+        float m = -INFINITY;  // reference max (lags the true max by < 2^8)
+        float l = 0.0f;
+        bool ok = true;
+        for (int t = 0; t < n_tiles; t++) {
+            // S_X(t) done also means PV_X(t-1) done: tcgen05.commit tracks all
+            // earlier MMAs of the issuing thread, so P_X and O_X are free.
+            if (!wait_or_abort(&s_full[X], (uint32_t)(t & 1), abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float sc[kN];
+            tmem_ld32(tS, sc);
+            tmem_ld32(tS + 32, sc + 32);
+            const int base = t * kN;
+            float mx = -INFINITY;
+            if (base + kN - 1 <= prefix + q0) {  // whole tile visible to every row of the CTA
+#pragma unroll
+                for (int j = 0; j < kN; j++) {
+                    sc[j] *= p.scale_log2;
+                    mx = fmaxf(mx, sc[j]);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < kN; j++) {
+                    sc[j] = (base + j <= row_limit) ? sc[j] * p.scale_log2 : -INFINITY;
+                    mx = fmaxf(mx, sc[j]);
+                }
+            }
+            const bool raise = mx > m + kRescaleAt;
+            float corr = 1.0f;
+            if (raise) {
+                corr = ex2f(m - mx);  // 0 on the first tile (m = -inf)
+                m = mx;
+                l *= corr;
+            }
+            if (t > 0 && __any_sync(0xffffffffu, raise)) {
+#pragma unroll
+                for (int c = 0; c < kD / 32; c++) {
+                    float ov[32];
+                    tmem_ld32(tO + c * 32, ov);
+#pragma unroll
+                    for (int j = 0; j < 32; j++) ov[j] *= corr;
+                    tmem_st32(tO + c * 32, ov);
+                }
+            }
+            const float mref = m == -INFINITY ? 0.0f : m;  // nothing visible yet: p = 0
+            float ls = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                float pv[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    pv[e] = ex2f(sc[c * 8 + e] - mref);
+                    ls += pv[e];
+                }
+                uint4 w = make_uint4(pack_bf16(pv[0], pv[1]), pack_bf16(pv[2], pv[3]), pack_bf16(pv[4], pv[5]),
+                                     pack_bf16(pv[6], pv[7]));
+                *reinterpret_cast<uint4*>(sP + swz(r, c)) = w;
+            }
+            l += ls;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            bar_arrive(&p_full[X]);
         }
-        if (t > 0 && __any_sync(0xffffffffu, raise)) {
+        // last PV of this tile, then the output row
+        if (ok && wait_or_abort(&pv_done[X], (uint32_t)((n_tiles - 1) & 1), abort_flag)) {
+            tc_fence_after();
+            const float inv = 1.0f / l;
+            float* orow = p.out + ((int64_t)(sm.q_start + q0 + qi) * p.Hq + h * G + g) * kD;
 #pragma unroll
             for (int c = 0; c < kD / 32; c++) {
                 float ov[32];
-                tmem_ld32(tmem + lane_base + kTmemO + c * 32, ov);
+                tmem_ld32(tO + c * 32, ov);
+                if (valid) {
 #pragma unroll
-                for (int j = 0; j < 32; j++) ov[j] *= corr;
-                tmem_st32(tmem + lane_base + kTmemO + c * 32, ov);
-            }
-        }
-        const float mref = m == -INFINITY ? 0.0f : m;  // a row with nothing visible yet keeps p = 0
-        float ls = 0.0f;
-        uint8_t* sP = sK + (t & 1) * kKBytes;
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-            float pv[8];
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                pv[e] = ex2f(sc[c * 8 + e] - mref);
-                ls += pv[e];
-            }
-            uint4 w = make_uint4(pack_bf16(pv[0], pv[1]), pack_bf16(pv[2], pv[3]), pack_bf16(pv[4], pv[5]),
-                                 pack_bf16(pv[6], pv[7]));
-            *reinterpret_cast<uint4*>(sP + swz(r, c)) = w;
-        }
-        l += ls;
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        tc_fence_before();
-        __syncthreads();
-        // 3. issue PV(t); then, once K(t+2)'s buffer is free, the next copy
-        //    and the scores two tiles ahead
-        if (tid == 0 && issue_ok) {
-            issue_pv(t);
-            pv_issued = t + 1;
-            issue_ok = bar_wait(&bars[4], (uint32_t)(t & 1));
-            pv_waited = t + 1;
-            if (issue_ok && t + 2 < n_tiles) {
-                issue_kv(t + 2);
-                kv_issued = t + 3;
-                issue_ok = bar_wait(&bars[(t + 2) & 1], (uint32_t)(((t + 2) >> 1) & 1));
-                kv_waited = t + 3;
-                if (issue_ok) issue_s(t + 2), s_issued = t + 3;
+                    for (int j = 0; j < 32; j += 4)
+                        *reinterpret_cast<float4*>(orow + c * 32 + j) =
+                            make_float4(ov[j] * inv, ov[j + 1] * inv, ov[j + 2] * inv, ov[j + 3] * inv);
+                }
             }
         }
     }
 
-    if (ok) {
-        // the last PV was waited for by thread 0; make it visible to all
-        ok = __syncthreads_and(issue_ok || tid != 0);
-    } else if (tid == 0) {
-        // Drain what is still in flight (bounded again) before TMEM and
-        // shared memory are released.
-        atomicOr(p.err, kErrTimeout);
-        for (int i = s_waited; i < s_issued; i++) bar_wait(&bars[2 + (i & 1)], (uint32_t)((i >> 1) & 1));
-        for (int i = pv_waited; i < pv_issued; i++) bar_wait(&bars[4], (uint32_t)(i & 1));
-        for (int i = kv_waited; i < kv_issued; i++) bar_wait(&bars[i & 1], (uint32_t)((i >> 1) & 1));
-    }
-    if (ok) {
-        tc_fence_after();
-        const float inv = 1.0f / l;
-        float* orow = p.out + ((int64_t)(sm.q_start + q0 + qi) * p.Hq + h * G + g) * kD;
-#pragma unroll
-        for (int c = 0; c < kD / 32; c++) {
-            float ov[32];
-            tmem_ld32(tmem + lane_base + kTmemO + c * 32, ov);
-            if (row_valid) {
-#pragma unroll
-                for (int j = 0; j < 32; j += 4)
-                    *reinterpret_cast<float4*>(orow + c * 32 + j) =
-                        make_float4(ov[j] * inv, ov[j + 1] * inv, ov[j + 2] * inv, ov[j + 3] * inv);
-            }
-        }
-    } else if (tid == 0) {
-        atomicOr(p.err, kErrTimeout);
-    }
     // ---- tear-down: every path frees TMEM ----
     tc_fence_before();
     __syncthreads();
+    if (tid == 0 && *abort_flag) atomicOr(p.err, kErrTimeout);
     if (warp == 0) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
@@ -471,6 +502,6 @@ int launch_prefill_tc(const PrefillParams& p, const CUtensorMap& tk, const CUten
     }
 }
 
-int prefill_queries_per_cta(int G) { return kM / G; }
+int prefill_queries_per_cta(int G) { return 2 * (kM / G); }
 
 }  // namespace s1kv
