@@ -347,15 +347,15 @@ def prefill_flops(prefix, suffixes, hq, d):
     return sum(4 * hq * d * (L * prefix + L * (L + 1) // 2) for L in suffixes)
 
 
-def run_cfg3(s1kv, torch, rank, reps=10):
+def run_cfg3(s1kv, torch, rank, reps=10, n=256):
     """cfg3: 256 sequences fork one 2050-token prefix (128 full blocks plus
     a 2-token tail, shared with refcounts); each appends a suffix of
     U[64, 512] tokens (seed 2), which first copies the shared tail block
     (copy-on-write), then runs the prefix-hit chunked prefill (tensor-core
     kernel), then 32 decode steps.  bf16 K/V, Hq 32 / Hkv 8 / D 128, block
     16; one layer (the workload names no layer count: figures are per
-    layer)."""
-    P, n, bs = 2050, 256, 16
+    layer).  `n` below 256 is a smaller profiling case of the same shape."""
+    P, bs = 2050, 16
     rng = np.random.default_rng(2)
     suff = [int(x) for x in rng.integers(64, 513, size=n)]
     dec_steps = 32
@@ -436,7 +436,7 @@ def run_ours(args):
             continue
         res[dtype] = run_variant(s1kv, torch, dtype, share, args.steps, args.warmup, rank, world,
                                  timed_e2e=not args.no_e2e, sample_clocks=(dtype == "f32"))
-    cfg3 = run_cfg3(s1kv, torch, rank) if not args.only or args.only == "cfg3" else None
+    cfg3 = run_cfg3(s1kv, torch, rank, n=args.cfg3_seqs) if not args.only or args.only == "cfg3" else None
     if args.only:
         # profiling case: one variant, no summary line
         if rank == 0 and args.only == "cfg3":
@@ -581,6 +581,7 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling cases only (the bench line uses 32)")
     ap.add_argument("--only", choices=["f32", "bf16", "cfg3"], help="profiling case: run one variant")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cfg3-seqs", type=int, default=256, help="profiling case: sequences of the cfg3 variant")
     args = ap.parse_args()
     globals()["LAYERS"] = args.layers
     if args.warmup < 3:

@@ -4,32 +4,33 @@
 // chunks longer than one token over bf16 K/V: row i of a sequence's q_len
 // new tokens attends to tokens 0 .. (kv_len - q_len) + i (:181).  This is a
 // dense QK^T / PV contraction, so it runs on the 5th-generation tensor
-// cores:
-//   * CTA = (sequence, query chunk, kv head).  Its M = 128 accumulator rows
-//     are (query, head) pairs: 128/G queries x the G query heads that share
-//     the KV head, so every K/V tile feeds all heads of the group.
+// cores, warp-specialised:
+//   * CTA = (sequence, query chunk, kv head), two query tiles A and B.  The
+//     M = 128 accumulator rows of a tile are (query, head) pairs: 128/G
+//     queries x the G query heads that share the KV head, so every K/V tile
+//     feeds all heads of the group, and both tiles share each K/V tile.
 //   * Q (fp32 in global) is narrowed to bf16 into shared memory in the
 //     128-byte-swizzled K-major layout UMMA reads.
-//   * K/V tiles of 64 tokens = 4 blocks are fetched through the block table
-//     by TMA (one 16-row x 64-element box per block and 128-byte half of a
-//     row, 128B swizzle, no multicast), double buffered, completion on
-//     mbarriers with bounded waits.
-//   * S = Q K^T (M 128, N 64, K 128) and O += P V (M 128, N 128, K 64) are
-//     tcgen05.mma kind::f16 with fp32 accumulators in TMEM: S double
-//     buffered (2 x 64 columns) so the scores of tile t+1 are computed while
-//     the threads run the softmax of tile t; O (128 columns) accumulates
-//     across all tiles.  256 columns per CTA, 2 CTAs per SM.  One thread
-//     issues; tcgen05.commit signals an mbarrier.
-//   * Each thread owns one accumulator row: it reads S with tcgen05.ld,
-//     applies the scale and the causal mask, runs the online softmax in the
-//     exp2 domain and writes P (bf16) in the swizzled K-major layout for the
-//     PV MMA into the current tile's K buffer (free once S is computed).
-//     The reference max only moves when the row max outgrows it by 2^8, and
-//     only then is the row of O in TMEM rescaled (tcgen05.ld/st), so the
-//     common tile does no per-row O work at all.
-// Every wait is bounded and decided for the whole CTA at once (a timeout
-// sets the device error word); copies in flight are drained and TMEM is
-// freed on every exit path.
+//   * K/V tiles of 128 tokens = 8 blocks come through the block table by
+//     TMA (one 16-row x 64-element box per block and 128-byte half of a
+//     row, 128B swizzle, no multicast), issued by 16 lanes of the producer
+//     warp in parallel into a 2-stage ring; completion on mbarriers.
+//   * One thread of the MMA warp issues S_X = Q_X K^T (M 128, N 128, K 128)
+//     and O_X += P_X V (M 128, N 128, K 128, A read from TMEM) as
+//     tcgen05.mma kind::f16 with fp32 accumulators in TMEM (512 columns:
+//     S_A, S_B, O_A, O_B).  Order PV_A(t) S_A(t+1) PV_B(t) S_B(t+1): a
+//     tile's next scores queue behind its PV, and one tile's softmax runs
+//     while the other tile's MMAs execute.
+//   * Two softmax warpgroups, one per tile; each thread owns one row: it
+//     reads its 128 scores with tcgen05.ld, masks the causal edge, runs the
+//     online softmax in the exp2 domain and writes P (bf16 pairs) back over
+//     the first 64 columns of its S with tcgen05.st, where the PV MMA reads
+//     it.  The reference max only moves when the row max outgrows it by
+//     2^8, and only then is the row of O in TMEM rescaled, so the common
+//     tile does no per-row O work.
+// Every wait is bounded; a timeout raises a CTA-wide abort flag that every
+// role polls, and the device error word.  Copies in flight are waited for
+// (bounded) and TMEM is freed on every exit path.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
@@ -43,28 +44,28 @@ namespace {
 
 constexpr uint32_t kSpin = 1u << 22;
 constexpr int kM = 128;          // accumulator rows per query tile (= TMEM lanes)
-constexpr int kN = 64;           // tokens per K/V tile
+constexpr int kN = 128;          // tokens per K/V tile
+constexpr int kBlocksPerTile = kN / 16;
 constexpr int kD = 128;          // head dim (two 64-element swizzle atoms)
-constexpr int kR = 3;            // K/V ring depth
+constexpr int kStages = 2;       // K/V ring depth
 constexpr int kSoftmaxThreads = 256;  // two warpgroups, one per query tile
 constexpr int kThreads = kSoftmaxThreads + 64;  // + TMA warp + MMA warp
-constexpr int kTmemCols = 512;   // S_A [0,64), S_B [64,128), O_A [128,256), O_B [256,384)
+constexpr int kTmemCols = 512;   // S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512)
+constexpr int kColO = 256;
 constexpr float kRescaleAt = 8.0f;  // log2 units: O is rescaled only when a row max grows by > 2^8
 
 // shared memory layout (bytes, 1024-aligned pieces)
 constexpr int kQBytes = 2 * kM * 128;          // one query tile: 2 atoms x 128 rows x 128 B = 32 KB
-constexpr int kPBytes = kM * 128;              // P of one query tile: 64 tokens x 128 rows = 16 KB
-constexpr int kKBytes = 2 * kN * 128;          // 2 atoms x 64 rows x 128 B = 16 KB
-constexpr int kVBytes = 2 * kN * 128;          // 2 d-atoms x 64 tokens x 128 B = 16 KB
+constexpr int kKBytes = 2 * kN * 128;          // 2 d-atoms x 128 tokens x 128 B = 32 KB
+constexpr int kVBytes = 2 * kN * 128;
 constexpr int kOffQ = 0;                        // Q_A, Q_B
-constexpr int kOffP = kOffQ + 2 * kQBytes;      // P_A, P_B
-constexpr int kOffK = kOffP + 2 * kPBytes;      // K ring
-constexpr int kOffV = kOffK + kR * kKBytes;     // V ring
-constexpr int kOffBar = kOffV + kR * kVBytes;
-// barriers: k_full[R], k_empty[R], v_full[R], v_empty[R], s_full[2], p_full[2], pv_done[2], drain
-constexpr int kNumBars = 4 * kR + 7;
+constexpr int kOffK = kOffQ + 2 * kQBytes;      // K ring
+constexpr int kOffV = kOffK + kStages * kKBytes;  // V ring
+constexpr int kOffBar = kOffV + kStages * kVBytes;
+// barriers: k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], pv_done[2], drain
+constexpr int kNumBars = 4 * kStages + 7;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;  // tmem slot, abort flag
-constexpr int kIdsCached = 256;                   // block ids of the first 64 tiles (4096 tokens)
+constexpr int kIdsCached = 256;                   // block ids of the first 32 tiles (4096 tokens)
 constexpr int kOffIds = (kOffMisc + 16 + 15) / 16 * 16;
 constexpr int kSmem = kOffIds + kIdsCached * 4 + 1024;  // + slack for 1024 alignment of the base
 
@@ -89,6 +90,9 @@ __device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t phase) {
     for (uint32_t i = 0; i < kSpin; i++)
         if (bar_try(b, phase)) return true;
     return false;
+}
+__device__ __forceinline__ void bar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
 }
 __device__ __forceinline__ void tma4(void* dst, const CUtensorMap* m, uint64_t* b, int c0, int c1, int c2, int c3) {
     asm volatile(
@@ -115,11 +119,20 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn_major, 
            ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, bool accumulate) {
+// D (TMEM) (+)= A (shared) * B (shared)
+__device__ __forceinline__ void mma_ss(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, bool accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(a), "l"(b), "r"(idesc), "r"((uint32_t)accumulate)
+        : "memory");
+}
+// D (TMEM) (+)= A (TMEM) * B (shared)
+__device__ __forceinline__ void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(b), "r"(idesc), "r"((uint32_t)accumulate)
         : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t* b) {
@@ -129,36 +142,70 @@ __device__ __forceinline__ void mma_commit(uint64_t* b) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// 32 consecutive fp32 columns of this thread's TMEM lane.
+// Loads 32 (or 128) consecutive fp32 columns of this thread's TMEM lane (one
+// instruction) and waits for them.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     uint32_t r[32];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
 #pragma unroll
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
-
-// Writes 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float* v) {
+    uint32_t r[128];
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
-        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
-        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
-        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
-        "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
-        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
-        "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]),
+        "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]),
+        "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]),
+        "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]),
+        "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]),
+        "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]),
+        "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]),
+        "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]),
+        "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+        : "r"(taddr)
         : "memory");
+#pragma unroll
+    for (int i = 0; i < 128; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Writes 32 (16) consecutive 32-bit columns of this thread's TMEM lane; the
+// _nowait form leaves tcgen05.wait::st to the caller.
+__device__ __forceinline__ void tmem_st32_nowait(uint32_t taddr, const float* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+        "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st16_nowait(uint32_t taddr, const float* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+    tmem_st32_nowait(taddr, v);
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
@@ -177,7 +224,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 // atom whose rows are 128 bytes: the chunk index is XORed with r mod 8.
 __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
-
 // Bounded wait that also gives up when another role of the CTA raised the
 // abort flag; a timeout raises it.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* b, uint32_t phase, volatile int* abort_flag) {
@@ -189,8 +235,10 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* b, uint32_t phase, volat
     return false;
 }
 
-__device__ __forceinline__ void bar_arrive(uint64_t* b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+// The same, decided for the whole warp: a lane that saw the abort flag takes
+// its warp with it (warp-collective tcgen05 instructions follow the waits).
+__device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t phase, volatile int* abort_flag) {
+    return __all_sync(0xffffffffu, wait_or_abort(b, phase, abort_flag));
 }
 
 }  // namespace
@@ -205,18 +253,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
     uint64_t* k_full = bars;
-    uint64_t* k_empty = bars + kR;
-    uint64_t* v_full = bars + 2 * kR;
-    uint64_t* v_empty = bars + 3 * kR;
-    uint64_t* s_full = bars + 4 * kR;       // [2]
-    uint64_t* p_full = bars + 4 * kR + 2;   // [2]
-    uint64_t* pv_done = bars + 4 * kR + 4;  // [2]
-    uint64_t* drain = bars + 4 * kR + 6;
+    uint64_t* k_empty = bars + kStages;
+    uint64_t* v_full = bars + 2 * kStages;
+    uint64_t* v_empty = bars + 3 * kStages;
+    uint64_t* s_full = bars + 4 * kStages;       // [2]
+    uint64_t* p_full = bars + 4 * kStages + 2;   // [2]
+    uint64_t* pv_done = bars + 4 * kStages + 4;  // [2]
+    uint64_t* drain = bars + 4 * kStages + 6;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
     int32_t* sIds = reinterpret_cast<int32_t*>(smem + kOffIds);
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int seq_i = blockIdx.x / p.max_chunks, chunk = blockIdx.x % p.max_chunks;
     const int h = blockIdx.y;
     const PrefillSeq sm = p.seqs[seq_i];
@@ -250,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return blk;
     };
-    for (int i = tid; i < min(n_tiles * (kN / 16), kIdsCached); i += kThreads) sIds[i] = lookup(i);
+    for (int i = tid; i < min(n_tiles * kBlocksPerTile, kIdsCached); i += kThreads) sIds[i] = lookup(i);
     // Q tiles (softmax threads): row r of tile X is head r / QT, query X*QT + r % QT.
     if (tid < kSoftmaxThreads) {
         const int X = tid >> 7, r = tid & 127;
@@ -276,64 +324,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == kSoftmaxThreads / 32) {
-        // ================= TMA producer: K/V ring, runs ahead =================
-        if ((tid & 31) == 0) {
-            for (int t = 0; t < n_tiles; t++) {
-                const int slot = t % kR, use = t / kR;
-                if (t >= kR && !wait_or_abort(&k_empty[slot], (uint32_t)((use - 1) & 1), abort_flag)) break;
-                uint8_t* kb = smem + kOffK + slot * kKBytes;
-                bar_expect(&k_full[slot], kKBytes);
-                for (int b = 0; b < kN / 16; b++) {
-                    const int i = t * (kN / 16) + b;
-                    const int32_t blk = i < kIdsCached ? sIds[i] : lookup(i);
-                    for (int a = 0; a < 2; a++)
-                        tma4(kb + a * (kN * 128) + b * 16 * 128, &tmK, &k_full[slot], a * 64, h, blk * 16, p.layer);
-                }
-                if (t >= kR && !wait_or_abort(&v_empty[slot], (uint32_t)((use - 1) & 1), abort_flag)) {
-                    // K(t) is in flight; drain it before leaving
-                    wait_or_abort(&k_full[slot], (uint32_t)(use & 1), abort_flag);
-                    break;
-                }
-                uint8_t* vb = smem + kOffV + slot * kVBytes;
-                bar_expect(&v_full[slot], kVBytes);
-                for (int b = 0; b < kN / 16; b++) {
-                    const int i = t * (kN / 16) + b;
-                    const int32_t blk = i < kIdsCached ? sIds[i] : lookup(i);
-                    for (int a = 0; a < 2; a++)
-                        tma4(vb + a * (kN * 128) + b * 16 * 128, &tmV, &v_full[slot], a * 64, h, blk * 16, p.layer);
-                }
-            }
+        // ================= TMA producer: K/V ring, 16 lanes issue =================
+        // lane L < 16 copies block L/2 of the tile, 64-element half L%2
+        const int b = lane >> 1, a = lane & 1;
+        int k_issued = 0, v_issued = 0;  // tiles whose K (V) copies were issued
+        for (int t = 0; t < n_tiles; t++) {
+            const int slot = t % kStages, use = t / kStages;
+            if (t >= kStages && !warp_wait(&k_empty[slot], (uint32_t)((use - 1) & 1), abort_flag)) break;
+            if (lane == 0) bar_expect(&k_full[slot], kKBytes);
+            __syncwarp();
+            const int i = t * kBlocksPerTile + b;
+            const int32_t blk = lane < 16 ? (i < kIdsCached ? sIds[i] : lookup(i)) : 0;
+            if (lane < 16)
+                tma4(smem + kOffK + slot * kKBytes + a * (kN * 128) + b * 16 * 128, &tmK, &k_full[slot], a * 64, h,
+                     blk * 16, p.layer);
+            k_issued = t + 1;
+            if (t >= kStages && !warp_wait(&v_empty[slot], (uint32_t)((use - 1) & 1), abort_flag)) break;
+            if (lane == 0) bar_expect(&v_full[slot], kVBytes);
+            __syncwarp();
+            if (lane < 16)
+                tma4(smem + kOffV + slot * kVBytes + a * (kN * 128) + b * 16 * 128, &tmV, &v_full[slot], a * 64, h,
+                     blk * 16, p.layer);
+            v_issued = t + 1;
         }
+        // every copy issued has landed before the CTA may exit (bounded)
+        for (int t = max(0, k_issued - kStages); t < k_issued; t++) bar_wait(&k_full[t % kStages], (uint32_t)((t / kStages) & 1));
+        for (int t = max(0, v_issued - kStages); t < v_issued; t++) bar_wait(&v_full[t % kStages], (uint32_t)((t / kStages) & 1));
     } else if (warp == kSoftmaxThreads / 32 + 1) {
         // ================= MMA issuer =================
-        if ((tid & 31) == 0) {
-            constexpr uint32_t idS = idesc_bf16(kM, kN, 0, 0);
-            constexpr uint32_t idO = idesc_bf16(kM, kD, 0, 1);
+        if (lane == 0) {
+            constexpr uint32_t idS = idesc_bf16(kM, kN, 0, 0);  // Q, K both K-major
+            constexpr uint32_t idO = idesc_bf16(kM, kD, 0, 1);  // P from TMEM, V MN-major
             const uint32_t qa[2] = {su32(smem + kOffQ), su32(smem + kOffQ + kQBytes)};
-            const uint32_t pa[2] = {su32(smem + kOffP), su32(smem + kOffP + kPBytes)};
             auto issue_s = [&](int X, int t) {
-                const uint32_t ka = su32(smem + kOffK + (t % kR) * kKBytes);
+                const uint32_t ka = su32(smem + kOffK + (t % kStages) * kKBytes);
 #pragma unroll
                 for (int ks = 0; ks < kD / 16; ks++) {
                     const uint32_t off = (ks & 3) * 32;  // 16 elements = 32 bytes inside a 128-byte atom row
                     const uint64_t da = sdesc(qa[X] + (ks >> 2) * (kM * 128) + off, 16, 1024);
                     const uint64_t db = sdesc(ka + (ks >> 2) * (kN * 128) + off, 16, 1024);
-                    mma_bf16(tmem + X * kN, da, db, idS, ks > 0);
+                    mma_ss(tmem + X * 128, da, db, idS, ks > 0);
                 }
                 mma_commit(&s_full[X]);
             };
             auto issue_pv = [&](int X, int t) {
-                const uint32_t va = su32(smem + kOffV + (t % kR) * kVBytes);
+                const uint32_t va = su32(smem + kOffV + (t % kStages) * kVBytes);
 #pragma unroll
                 for (int ks = 0; ks < kN / 16; ks++) {
-                    const uint64_t da = sdesc(pa[X] + ks * 32, 16, 1024);
+                    // P: 16 tokens = 8 columns of bf16 pairs; V: 16 token rows = 2 KB
                     const uint64_t db = sdesc(va + ks * 16 * 128, kN * 128, 1024);
-                    mma_bf16(tmem + 128 + X * 128, da, db, idO, t > 0 || ks > 0);
+                    mma_ts(tmem + kColO + X * 128, tmem + X * 128 + ks * 8, db, idO, t > 0 || ks > 0);
                 }
                 mma_commit(&pv_done[X]);
             };
-            // Tensor-core order: S_A0 S_B0 | PV_A0 S_A1 PV_B0 S_B1 | PV_A1 S_A2 ...
-            // so one warpgroup's softmax always overlaps the other's MMAs.
             bool ok = wait_or_abort(&k_full[0], 0, abort_flag);
             if (ok) {
                 tc_fence_after();
@@ -342,16 +385,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mma_commit(&k_empty[0]);
             }
             for (int t = 0; t < n_tiles && ok; t++) {
-                const int slot = t % kR;
+                const int slot = t % kStages;
+                const bool more = t + 1 < n_tiles;
+                const int ns = (t + 1) % kStages;
                 ok = wait_or_abort(&p_full[0], (uint32_t)(t & 1), abort_flag) &&
-                     wait_or_abort(&v_full[slot], (uint32_t)((t / kR) & 1), abort_flag);
+                     wait_or_abort(&v_full[slot], (uint32_t)((t / kStages) & 1), abort_flag);
                 if (!ok) break;
                 tc_fence_after();
                 issue_pv(0, t);
-                const bool more = t + 1 < n_tiles;
-                const int ns = (t + 1) % kR;
-                if (more) {
-                    ok = wait_or_abort(&k_full[ns], (uint32_t)(((t + 1) / kR) & 1), abort_flag);
+                if (more) {  // S_A(t+1) overwrites P_A(t): issued after PV_A(t), which reads it first
+                    ok = wait_or_abort(&k_full[ns], (uint32_t)(((t + 1) / kStages) & 1), abort_flag);
                     if (!ok) break;
                     issue_s(0, t + 1);
                 }
@@ -376,38 +419,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool valid = q0 + qi < sm.q_len;
         const int row_limit = prefix + q0 + qi;  // last visible token
         const uint32_t lane_base = (uint32_t)(32 * ((tid >> 5) & 3)) << 16;
-        const uint32_t tS = tmem + lane_base + X * kN;
-        const uint32_t tO = tmem + lane_base + 128 + X * 128;
-        uint8_t* sP = smem + kOffP + X * kPBytes;
+        const uint32_t tS = tmem + lane_base + X * 128;  // S_X, P_X over its first 64 columns
+        const uint32_t tO = tmem + lane_base + kColO + X * 128;
         float m = -INFINITY;  // reference max (lags the true max by < 2^8)
         float l = 0.0f;
         bool ok = true;
         for (int t = 0; t < n_tiles; t++) {
-            // S_X(t) done also means PV_X(t-1) done: tcgen05.commit tracks all
-            // earlier MMAs of the issuing thread, so P_X and O_X are free.
-            if (!wait_or_abort(&s_full[X], (uint32_t)(t & 1), abort_flag)) {
+            // S_X(t) done also means PV_X(t-1) done (tcgen05.commit tracks every
+            // earlier MMA of the issuing thread): O_X and P_X are free.
+            if (!warp_wait(&s_full[X], (uint32_t)(t & 1), abort_flag)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             float sc[kN];
-            tmem_ld32(tS, sc);
-            tmem_ld32(tS + 32, sc + 32);
+            tmem_ld128(tS, sc);
             const int base = t * kN;
-            float mx = -INFINITY;
-            if (base + kN - 1 <= prefix + q0) {  // whole tile visible to every row of the CTA
+            if (base + kN - 1 > prefix + q0) {  // tile crosses the causal edge of some row
 #pragma unroll
-                for (int j = 0; j < kN; j++) {
-                    sc[j] *= p.scale_log2;
-                    mx = fmaxf(mx, sc[j]);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < kN; j++) {
-                    sc[j] = (base + j <= row_limit) ? sc[j] * p.scale_log2 : -INFINITY;
-                    mx = fmaxf(mx, sc[j]);
-                }
+                for (int j = 0; j < kN; j++)
+                    if (base + j > row_limit) sc[j] = -INFINITY;
             }
+            // Row max of the raw scores over four independent chains; rounding
+            // is monotonic, so max(s) * scale equals max(s * scale) exactly.
+            float m4[4] = {sc[0], sc[1], sc[2], sc[3]};
+#pragma unroll
+            for (int j = 4; j < kN; j++) m4[j & 3] = fmaxf(m4[j & 3], sc[j]);
+            const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
             const bool raise = mx > m + kRescaleAt;
             float corr = 1.0f;
             if (raise) {
@@ -415,41 +453,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                 m = mx;
                 l *= corr;
             }
-            if (t > 0 && __any_sync(0xffffffffu, raise)) {
+            const float mref = m == -INFINITY ? 0.0f : m;  // nothing visible yet: p = 0
+            // p = 2^(s * scale - mref): one packed FFMA per pair, then ex2
+            const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-mref, -mref);
+            float2 ls2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
+            for (int q = 0; q < 4; q++) {
+                float pk[16];
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+                    const int j = q * 32 + 2 * e;
+                    const float2 x = __ffma2_rn(make_float2(sc[j], sc[j + 1]), sc2, nm2);
+                    const float2 pv = make_float2(ex2f(x.x), ex2f(x.y));
+                    ls2[e & 1] = __fadd2_rn(ls2[e & 1], pv);
+                    pk[e] = __uint_as_float(pack_bf16(pv.x, pv.y));
+                }
+                tmem_st16_nowait(tS + q * 16, pk);
+            }
+            // rescale O_X (the scores are dead by now: no register pressure)
+            if (t > 0 && __any_sync(0xffffffffu, raise)) {
+#pragma unroll 1
                 for (int c = 0; c < kD / 32; c++) {
                     float ov[32];
                     tmem_ld32(tO + c * 32, ov);
 #pragma unroll
                     for (int j = 0; j < 32; j++) ov[j] *= corr;
-                    tmem_st32(tO + c * 32, ov);
+                    tmem_st32_nowait(tO + c * 32, ov);
                 }
             }
-            const float mref = m == -INFINITY ? 0.0f : m;  // nothing visible yet: p = 0
-            float ls = 0.0f;
-#pragma unroll
-            for (int c = 0; c < 8; c++) {
-                float pv[8];
-#pragma unroll
-                for (int e = 0; e < 8; e++) {
-                    pv[e] = ex2f(sc[c * 8 + e] - mref);
-                    ls += pv[e];
-                }
-                uint4 w = make_uint4(pack_bf16(pv[0], pv[1]), pack_bf16(pv[2], pv[3]), pack_bf16(pv[4], pv[5]),
-                                     pack_bf16(pv[6], pv[7]));
-                *reinterpret_cast<uint4*>(sP + swz(r, c)) = w;
-            }
-            l += ls;
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            l += (ls2[0].x + ls2[1].x) + (ls2[0].y + ls2[1].y);
             tc_fence_before();
             bar_arrive(&p_full[X]);
         }
         // last PV of this tile, then the output row
-        if (ok && wait_or_abort(&pv_done[X], (uint32_t)((n_tiles - 1) & 1), abort_flag)) {
+        if (ok && warp_wait(&pv_done[X], (uint32_t)((n_tiles - 1) & 1), abort_flag)) {
             tc_fence_after();
             const float inv = 1.0f / l;
             float* orow = p.out + ((int64_t)(sm.q_start + q0 + qi) * p.Hq + h * G + g) * kD;
-#pragma unroll
+#pragma unroll 1
             for (int c = 0; c < kD / 32; c++) {
                 float ov[32];
                 tmem_ld32(tO + c * 32, ov);
