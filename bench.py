@@ -416,6 +416,102 @@ def run_cfg3(s1kv, torch, rank, reps=10, n=256):
             "decode_tok_s_per_layer": n / (dec_ms * 1e-3)}
 
 
+CFG4_B, CFG4_CTX, CFG4_HQ, CFG4_HKV, CFG4_LAYERS = 4, 131072, 64, 8, 80
+
+
+def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3):
+    """cfg4, KV-head-sharded long-context decode: 4 sequences at context
+    131072, Hq 64 / Hkv 8 / D 128, bf16 K/V, 80 layers, blocks scattered over
+    a pool of 1.1x need (permutation seed 3).  Rank r of N keeps only KV heads
+    [8r/N, 8(r+1)/N) (s1kv.head_shard).  Each layer of a step: RoPE + append
+    of the new token, paged decode of the local heads, one all-gather of the
+    [4, 64/N, 128] outputs (NCCL over NVLink) and the head-major to
+    token-major reorder.  The next layer's queries for this rank's heads are
+    another rank's outputs, so the gather is on the critical path as it is in
+    a model.  Where 80 layers of the pool do not fit in one GPU's memory
+    (N = 1), fewer layers are timed and the step figures are scaled to 80.
+    K/V are seeded normal values (synthetic post-RoPE keys)."""
+    B, CTX, hq_all, hkv_all = CFG4_B, CFG4_CTX, CFG4_HQ, CFG4_HKV
+    kv_lo, kv_hi, q_lo, q_hi = s1kv.head_shard(world, rank, hkv_all, hq_all)
+    hkv, hq = kv_hi - kv_lo, q_hi - q_lo
+    need = B * ((CTX + steps + warmup + 2 + BS - 1) // BS)
+    max_blocks = int(need * 1.1)
+    per_layer = max_blocks * BS * hkv * D * 2 * 2
+    torch.cuda.empty_cache()
+    free, _ = torch.cuda.mem_get_info()
+    layers = int(min(CFG4_LAYERS, (free - 16e9) // per_layer))
+    layers = int(-max_over_ranks(torch, world, -layers))  # every rank times the same layers
+    order = np.random.default_rng(3).permutation(max_blocks).astype(np.int32)
+    pool = s1kv.Pool(layers, hkv, D, max_blocks, BS, dtype="bf16", initial_free_list=order, max_seqs=8)
+    gen = torch.Generator(device="cuda").manual_seed(31 + rank)
+    seqs = list(range(B))
+    with pool.batch(seqs, [CTX] * B, [0] * B) as b:
+        kbuf = torch.empty((B * CTX, hkv, D), device="cuda")
+        vbuf = torch.empty_like(kbuf)
+        for layer in range(layers):
+            kbuf.normal_(generator=gen)
+            vbuf.normal_(generator=gen)
+            b.append(layer, kbuf, vbuf)
+        del kbuf, vbuf
+    torch.cuda.synchronize()
+    q0 = torch.randn((B, hq, D), device="cuda", generator=gen)
+    kn = torch.randn((layers, B, hkv, D), device="cuda", generator=gen)
+    vn = torch.randn((layers, B, hkv, D), device="cuda", generator=gen)
+    q_rot = torch.empty((B, hq, D), device="cuda")
+    out = torch.empty((B, hq, D), device="cuda")
+    gbuf = torch.empty((world, B, hq, D), device="cuda")
+    nxt = (rank + 1) % world
+
+    def step(ev=None):
+        q = q0
+        with pool.batch(seqs, [1] * B) as bt:
+            for layer in range(layers):
+                bt.rope_append(layer, kn[layer], vn[layer], q=q, q_out=q_rot)
+                if ev is not None:
+                    ev[layer][0].record()
+                bt.attention(layer, q_rot, out=out)
+                if ev is not None:
+                    ev[layer][1].record()
+                full = s1kv.gather_heads(out, world, buf=gbuf)  # [B, 64, 128] token-major on every rank
+                if ev is not None:
+                    ev[layer][2].record()
+                q = full[:, nxt * hq:(nxt + 1) * hq].contiguous()
+
+    for _ in range(warmup):
+        step()
+    barrier(torch, world)
+    torch.cuda.synchronize()
+    ctx_before = [pool.length(s) for s in seqs]
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(layers)] for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(steps):
+        step(evs[i])
+    t1.record()
+    torch.cuda.synchronize()
+    elapsed = max_over_ranks(torch, world, t0.elapsed_time(t1))
+    attn_ms = float(np.mean([evs[i][l][0].elapsed_time(evs[i][l][1]) for i in range(steps) for l in range(layers)]))
+    gather_ms = float(np.mean([evs[i][l][1].elapsed_time(evs[i][l][2]) for i in range(steps) for l in range(layers)]))
+    attn_ms = max_over_ranks(torch, world, attn_ms)
+    gather_ms = max_over_ranks(torch, world, gather_ms)
+    # algorithmic bytes of one layer's attention on this GPU: K and V of the
+    # local heads once, q in and out (fp32), block ids
+    ctx_mid = [c + (steps + 1) // 2 for c in ctx_before]
+    attn_bytes = (sum(ctx_mid) * 2 * hkv * D * 2 + B * hq * D * (4 + 4) + sum((c + BS - 1) // BS for c in ctx_mid) * 4)
+    assert pool.check_device() == 0
+    pool.close()
+    del q0, kn, vn, q_rot, out, gbuf
+    torch.cuda.empty_cache()
+    step_ms_80 = elapsed / steps * CFG4_LAYERS / layers
+    return {"workload": "cfg4: 4 seqs x ctx 131072, Hq64/Hkv8/D128, bf16, 80 layers, pool 1.1x scattered (seed 3)",
+            "parallelism": f"kv-head-sharded x{world} ({hkv} KV heads per GPU), NCCL all-gather per layer",
+            "scaling": "strong", "layers_timed": layers, "steps": steps,
+            "ms_per_step_80_layers": step_ms_80, "tok_s": B / (step_ms_80 * 1e-3),
+            "ms_per_layer": elapsed / steps / layers, "attn_ms_per_layer": attn_ms,
+            "allgather_reorder_ms_per_layer": gather_ms,
+            "attn_bytes_per_layer_per_gpu": attn_bytes, "kv_gbs_per_gpu": attn_bytes / (attn_ms * 1e-3) / 1e9}
+
+
 def run_ours(args):
     import torch
     import s1kv
@@ -437,14 +533,19 @@ def run_ours(args):
         res[dtype] = run_variant(s1kv, torch, dtype, share, args.steps, args.warmup, rank, world,
                                  timed_e2e=not args.no_e2e, sample_clocks=(dtype == "f32"))
     cfg3 = run_cfg3(s1kv, torch, rank, n=args.cfg3_seqs) if not args.only or args.only == "cfg3" else None
+    cfg4 = run_cfg4(s1kv, torch, rank, world) if not args.only or args.only == "cfg4" else None
     if args.only:
         # profiling case: one variant, no summary line
-        if rank == 0 and args.only == "cfg3":
-            print(json.dumps({"profiling_case": "cfg3", **cfg3}))
+        if rank == 0 and args.only in ("cfg3", "cfg4"):
+            print(json.dumps({"profiling_case": args.only, **(cfg3 if args.only == "cfg3" else cfg4)}))
         elif rank == 0:
             r = res[args.only]
             print(json.dumps({"profiling_case": args.only, "layers": LAYERS, "ms_per_step": r["elapsed_ms"] / args.steps,
                               "avg_launch_ms": r["avg_launch_ms"], "bytes_per_launch": r["bytes_per_launch"]}))
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
         return
     h = res["f32"]
     elapsed = max_over_ranks(torch, world, h["elapsed_ms"])
@@ -512,7 +613,10 @@ def run_ours(args):
                              "peak_source": tflops_src},
                 "prefill_attn_ms_per_layer": cfg3["prefill_attn_ms"], "prefill_flops_per_layer": cfg3["prefill_flops"],
                 "prefill_step_ms_per_layer": cfg3["prefill_step_ms"], "cow_copies": cfg3["cow_copies"],
-                "decode_ms_per_step_per_layer": cfg3["decode_ms_per_step"]}},
+                "decode_ms_per_step_per_layer": cfg3["decode_ms_per_step"]},
+            "cfg4_head_sharded": None if cfg4 is None else {
+                **cfg4, "roofline": {"bound": "hbm", "achieved": cfg4["kv_gbs_per_gpu"], "peak": peak,
+                                     "frac": cfg4["kv_gbs_per_gpu"] / peak, "unit": "GB/s"}}},
         "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
     }
     print(json.dumps(line))
@@ -579,7 +683,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling cases only (the bench line uses 32)")
-    ap.add_argument("--only", choices=["f32", "bf16", "cfg3"], help="profiling case: run one variant")
+    ap.add_argument("--only", choices=["f32", "bf16", "cfg3", "cfg4"], help="profiling case: run one variant")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cfg3-seqs", type=int, default=256, help="profiling case: sequences of the cfg3 variant")
     args = ap.parse_args()

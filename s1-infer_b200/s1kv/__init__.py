@@ -486,3 +486,45 @@ def apply_rope(x, start_pos=0, theta=1.0e6, device=None):
         check(lib().s1kv_apply_rope(_dptr(x3), _dptr(out), start_pos, x3.shape[0], x3.shape[1], x3.shape[2], theta,
                                     _stream()))
     return out.reshape(shape)
+
+
+# ================================================ KV-head-sharded serving ==
+# Long-context requests are split across GPUs by KV head: rank r of `world`
+# keeps a pool holding only KV heads [kv_lo, kv_hi) of every token (and runs
+# the query heads of those groups); after each layer's attention one
+# all-gather over NVLink gives every rank the outputs of all heads.  No
+# reference counterpart: s1-infer runs on one host thread.
+
+def head_shard(world, rank, num_kv_heads, num_q_heads):
+    """(kv_lo, kv_hi, q_lo, q_hi): the KV heads and query heads rank `rank`
+    of `world` owns.  Whole GQA groups stay together (query head h reads KV
+    head h // (Hq / Hkv)), so every rank runs the unchanged kernels on a
+    pool of num_kv_heads / world heads."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} of world {world}")
+    if num_kv_heads % world or num_q_heads % num_kv_heads:
+        raise ValueError(f"{num_kv_heads} KV heads / {num_q_heads} query heads do not split over {world} ranks")
+    kv = num_kv_heads // world
+    q = num_q_heads // world
+    return rank * kv, (rank + 1) * kv, rank * q, (rank + 1) * q
+
+
+def gather_heads(out_local, world, group=None, buf=None):
+    """All-gather of per-rank attention outputs [B, Hq/world, D] into the
+    token-major [B, Hq, D] every rank needs for the output projection: one
+    collective (NCCL all_gather_into_tensor over NVLink on GPUs, gloo on
+    CPU) into a head-major buffer [world, B, Hq/world, D], then the
+    head-major to token-major reorder.  `buf` (optional) is that buffer."""
+    import torch
+    import torch.distributed as dist
+    B, hq_l, D = out_local.shape
+    if world == 1:
+        return out_local
+    src = out_local.contiguous()
+    if buf is None:
+        buf = torch.empty((world, B, hq_l, D), dtype=src.dtype, device=src.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(buf, src, group=group)
+    else:
+        dist.all_gather(list(buf.unbind(0)), src, group=group)
+    return buf.transpose(0, 1).reshape(B, world * hq_l, D)

@@ -1,0 +1,79 @@
+"""KV-head-sharded decode on two GPUs (one process per GPU, NCCL): each
+rank's pool holds half of the KV heads of every token (bf16 storage), runs
+the paged decode kernel for the query heads of its groups, and one NCCL
+all-gather over NVLink reassembles all heads.  The gathered output is
+compared with the oracle's full-head GQA attention on the same bf16-rounded
+K/V (tolerance 2e-5 x max |ref|, as for the 1-GPU bf16 path).  Skipped on
+a box with fewer than two GPUs."""
+import datetime
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, out_dir):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "s1-infer_b200"))
+    import torch
+    import torch.distributed as dist
+
+    import s1kv
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    Hq, Hkv, D, bs = 32, 8, 128, 16
+    ctx = [300, 517, 1024]
+    B = len(ctx)
+    rng = np.random.default_rng(7)
+    k = [rng.standard_normal((c, Hkv, D), dtype=np.float32) for c in ctx]
+    v = [rng.standard_normal((c, Hkv, D), dtype=np.float32) for c in ctx]
+    q = rng.standard_normal((B, Hq, D), dtype=np.float32)
+    kv_lo, kv_hi, q_lo, q_hi = s1kv.head_shard(world, rank, Hkv, Hq)
+    need = sum((c + bs - 1) // bs for c in ctx)
+    pool = s1kv.Pool(1, kv_hi - kv_lo, D, need + 4, bs, dtype="bf16",
+                     initial_free_list=np.random.default_rng(3).permutation(need + 4))
+    seqs = list(range(B))
+    with pool.batch(seqs, ctx, [0] * B) as b:
+        b.append(0, torch.from_numpy(np.concatenate([x[:, kv_lo:kv_hi] for x in k])).cuda().contiguous(),
+                 torch.from_numpy(np.concatenate([x[:, kv_lo:kv_hi] for x in v])).cuda().contiguous())
+    out_local = pool.attention(0, seqs, [1] * B, torch.from_numpy(q[:, q_lo:q_hi].copy()).cuda(), q_hi - q_lo)
+    full = s1kv.gather_heads(out_local, world)
+    torch.cuda.synchronize()
+    assert pool.check_device() == 0
+    pool.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    np.save(os.path.join(out_dir, f"rank{rank}.npy"), full.cpu().numpy())
+
+
+@pytest.mark.gpu
+def test_two_gpu_head_sharded_decode_matches_oracle(tmp_path, oracle):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    world = 2
+    mp.start_processes(_rank, args=(world, _port(), str(tmp_path)), nprocs=world, start_method="spawn", join=True)
+    Hq, Hkv, D = 32, 8, 128
+    ctx = [300, 517, 1024]
+    rng = np.random.default_rng(7)
+    k = [rng.standard_normal((c, Hkv, D), dtype=np.float32) for c in ctx]
+    v = [rng.standard_normal((c, Hkv, D), dtype=np.float32) for c in ctx]
+    q = rng.standard_normal((len(ctx), Hq, D), dtype=np.float32)
+    ref = np.stack([oracle.gqa_attention(q[s:s + 1], oracle.bf16_round(k[s]), oracle.bf16_round(v[s]), Hq, Hkv, D)[0]
+                    for s in range(len(ctx))])
+    for r in range(world):
+        got = np.load(tmp_path / f"rank{r}.npy")
+        assert got.shape == ref.shape
+        assert np.max(np.abs(got - ref)) <= 2e-5 * np.max(np.abs(ref))

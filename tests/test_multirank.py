@@ -81,3 +81,56 @@ def test_two_rank_gloo_sharded_pools(tmp_path):
         assert tokens == sum(sum(s) for s in shares)
         assert slowest == world
         assert n_all == world * bench.SEQS_PER_GPU
+
+
+def _head_rank_main(rank, world, port, out_dir):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "s1-infer_b200"))
+    import torch
+    import torch.distributed as dist
+
+    import s1kv
+    from oracle import oracle
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    Hq, Hkv, D, B = 16, 4, 64, 3
+    rng = np.random.default_rng(11)
+    ctx = [37, 90, 64]
+    k = [rng.standard_normal((c, Hkv, D), dtype=np.float32) for c in ctx]
+    v = [rng.standard_normal((c, Hkv, D), dtype=np.float32) for c in ctx]
+    q = rng.standard_normal((B, Hq, D), dtype=np.float32)
+    kv_lo, kv_hi, q_lo, q_hi = s1kv.head_shard(world, rank, Hkv, Hq)
+    # this rank's share: its KV heads and the query heads of their groups
+    local = np.stack([oracle.gqa_attention(q[s:s + 1, q_lo:q_hi], k[s][:, kv_lo:kv_hi], v[s][:, kv_lo:kv_hi],
+                                           q_hi - q_lo, kv_hi - kv_lo, D)[0] for s in range(B)])
+    full = s1kv.gather_heads(torch.from_numpy(local), world).numpy()
+    ref = np.stack([oracle.gqa_attention(q[s:s + 1], k[s], v[s], Hq, Hkv, D)[0] for s in range(B)])
+    dist.barrier()
+    dist.destroy_process_group()
+    np.save(os.path.join(out_dir, f"head{rank}.npy"), np.stack([full, ref]))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_head_sharded_gather_reassembles_full_attention(tmp_path, world):
+    """KV-head sharding: each gloo rank computes the attention of its own KV
+    heads' groups; the all-gather and head-major to token-major reorder give
+    every rank exactly the full-head result."""
+    import torch.multiprocessing as mp
+    mp.start_processes(_head_rank_main, args=(world, free_port(), str(tmp_path)), nprocs=world, start_method="spawn",
+                       join=True)
+    for r in range(world):
+        full, ref = np.load(tmp_path / f"head{r}.npy")
+        assert np.array_equal(full, ref)
+
+
+def test_head_shard_partition():
+    sys.path.insert(0, os.path.join(ROOT, "s1-infer_b200"))
+    import s1kv
+    for world in (1, 2, 4, 8):
+        parts = [s1kv.head_shard(world, r, 8, 64) for r in range(world)]
+        assert [p[0] for p in parts] == list(range(0, 8, 8 // world))
+        assert parts[-1][1] == 8 and parts[-1][3] == 64
+        for kv_lo, kv_hi, q_lo, q_hi in parts:  # whole GQA groups
+            assert q_lo == kv_lo * 8 and q_hi == kv_hi * 8
+    with pytest.raises(ValueError):
+        s1kv.head_shard(3, 0, 8, 64)
