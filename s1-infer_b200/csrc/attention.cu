@@ -623,6 +623,15 @@ int launch_attention_generic(const AttnParams& p, int dtype, cudaStream_t stream
 int launch_attention(s1kv_pool* pool, const AttnParams& p, int dtype, cudaStream_t stream) {
     if (p.n_rows <= 0) return S1KV_OK;
     const int G = p.Hq / p.Hkv;
+    if (p.table && pool->tmap_sw_ok && p.items && decode_mma_supported(dtype, p.D, G, p.block_size)) {
+        // bf16 K/V, head_dim 128: tensor-core decode, then the shared combine
+        int st = launch_decode_mma(p, pool->tmap_k_sw, pool->tmap_v_sw, stream);
+        if (st) return st;
+        combine_kernel<<<dim3((unsigned)p.n_rows, (unsigned)p.Hkv), 128, 0, stream>>>(p, G);
+        g_launches++;
+        S1KV_CUDA(cudaGetLastError());
+        return S1KV_OK;
+    }
     if (p.table && pool->tmap_ok && p.items && tma_attention_supported(dtype, p.D, G, p.block_size)) {
         if (dtype == S1KV_DTYPE_F32)
             return p.D == 128 ? launch_decode_g<float, 128>(pool, p, G, stream)

@@ -290,6 +290,11 @@ int encode_kv_maps(const void* k, const void* v, int dtype, int Hkv, int D, int6
 int launch_decode_with_maps(const AttnParams& p, const CUtensorMap& tk, const CUtensorMap& tv, int dtype,
                             cudaStream_t stream);
 
+// Tensor-core (mma.sync) decode over bf16 K/V, head_dim 128 (decode_mma.cu):
+// partials in the same format as the CUDA-core decode kernel.
+bool decode_mma_supported(int dtype, int D, int G, int block_size);
+int launch_decode_mma(const AttnParams& p, const CUtensorMap& tk_sw, const CUtensorMap& tv_sw, cudaStream_t stream);
+
 // Tensor-core prefix-hit prefill (prefill_tc.cu).
 bool prefill_tc_supported(int dtype, int D, int G, int block_size);
 int prefill_queries_per_cta(int G);
