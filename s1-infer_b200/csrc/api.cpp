@@ -332,6 +332,13 @@ int s1kv_batch_attention(s1kv_batch* b, int32_t layer, const float* q, float* ou
     ap.layer = layer;
     ap.scale_log2 = scale_log2(D);
     ap.err = p->d_err;
+    const size_t cbytes = (size_t)b->n_rows * Hkv * sizeof(int32_t);
+    if (p->counters.cap < cbytes) {
+        st = p->counters.ensure(cbytes);
+        if (st) return st;
+        S1KV_CUDA(cudaMemsetAsync(p->counters.p, 0, p->counters.cap, stream));
+    }
+    ap.counters = (int32_t*)p->counters.p;
     return launch_attention(p, ap, p->desc.dtype, stream);
 }
 

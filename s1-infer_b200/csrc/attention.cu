@@ -41,6 +41,7 @@
 #include <cfloat>
 #include <cmath>
 
+#include "combine.cuh"
 #include "internal.h"
 
 namespace s1kv {
@@ -145,7 +146,7 @@ struct DecodeCfg {
     static constexpr int kNS = S::kNS;                                // stages per warp
     static constexpr int kPFloats = (kTile * kNV + kNV + 3) / 4 * 4;  // p[tile][head] + corr[head]
     static constexpr int kRing = kNW * kNS * kStageBytes;
-    static constexpr int kSmem = kRing + kNW * kPFloats * 4 + kNW * kNS * 8;
+    static constexpr int kSmem = kRing + kNW * kPFloats * 4 + kNW * kNS * 8 + 16;  // + last-CTA flag
     static_assert(kNCH % kLPT == 0, "chunks must split evenly over lanes");
     static_assert(kLPT >= 8, "a quarter-warp phase must read 8 distinct chunks");
     static_assert((1 << kH) <= kLPT, "one halving level per lane bit");
@@ -470,31 +471,17 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, 
             }
         }
     }
+    if (p.counters && rm.n_split > 1)
+        finish_split_row(p, item.row, h, rm.n_split, G, D,
+                         reinterpret_cast<int*>(smem + C::kRing + NW * C::kPFloats * 4 + NW * NS * 8));
 }
 
-// Combines the split partials of multi-split rows: rescale to the global
-// max, sum, normalise.
+// Combines the split partials of multi-split rows (separate pass, for
+// launches without arrival counters): rescale to the global max, sum,
+// normalise.
 __global__ void combine_kernel(const AttnParams p, int G) {
-    const RowMeta rm = p.rows[blockIdx.x];
-    if (rm.n_split <= 1) return;
-    const int h = blockIdx.y, D = p.D;
-    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-        const int g = idx / D, d = idx % D;
-        float M = -INFINITY;
-        for (int s = 0; s < rm.n_split; s++) {
-            const int64_t part = (int64_t)(rm.part_off + s) * p.Hkv + h;
-            M = fmaxf(M, p.part_ml[(part * G + g) * 2]);
-        }
-        float L = 0.0f, O = 0.0f;
-        for (int s = 0; s < rm.n_split; s++) {
-            const int64_t part = (int64_t)(rm.part_off + s) * p.Hkv + h;
-            const float ms = p.part_ml[(part * G + g) * 2];
-            const float f = (ms == -INFINITY) ? 0.0f : ex2(ms - M);
-            L = fmaf(p.part_ml[(part * G + g) * 2 + 1], f, L);
-            O = fmaf(p.part_o[(part * G + g) * D + d], f, O);
-        }
-        p.out[((int64_t)blockIdx.x * p.Hq + h * G + g) * D + d] = O / L;
-    }
+    if (p.rows[blockIdx.x].n_split <= 1) return;
+    combine_partials(p, blockIdx.x, blockIdx.y, G, p.D, threadIdx.x, blockDim.x);
 }
 
 // ------------------------------------------------------------ generic ----
@@ -586,8 +573,7 @@ static int launch_decode_t(s1kv_pool* pool, const AttnParams& p, cudaStream_t st
     decode_tma_kernel<T, D, G><<<grid, C::kNW * 32, C::kSmem, stream>>>(p, pool->tmap_k, pool->tmap_v);
     g_launches++;
     S1KV_CUDA(cudaGetLastError());
-    bool any_multi = true;  // combine exits early for single-split rows
-    if (any_multi) {
+    if (!p.counters) {  // otherwise the last CTA of each split row merged it; combine exits early for single-split rows
         combine_kernel<<<dim3((unsigned)p.n_rows, (unsigned)p.Hkv), 128, 0, stream>>>(p, G);
         g_launches++;
         S1KV_CUDA(cudaGetLastError());
@@ -626,7 +612,7 @@ int launch_attention(s1kv_pool* pool, const AttnParams& p, int dtype, cudaStream
     if (p.table && pool->tmap_sw_ok && p.items && decode_mma_supported(dtype, p.D, G, p.block_size)) {
         // bf16 K/V, head_dim 128: tensor-core decode, then the shared combine
         int st = launch_decode_mma(p, pool->tmap_k_sw, pool->tmap_v_sw, stream);
-        if (st) return st;
+        if (st || p.counters) return st;
         combine_kernel<<<dim3((unsigned)p.n_rows, (unsigned)p.Hkv), 128, 0, stream>>>(p, G);
         g_launches++;
         S1KV_CUDA(cudaGetLastError());

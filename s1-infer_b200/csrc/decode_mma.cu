@@ -34,6 +34,7 @@
 
 #include <cmath>
 
+#include "combine.cuh"
 #include "internal.h"
 
 namespace s1kv {
@@ -50,7 +51,7 @@ constexpr int kBoxBytes = kTile * 128;         // 16 tokens x 64 bf16, 128B-swiz
 constexpr int kTileBytes = 2 * kBoxBytes;      // K (or V) of one tile: 4 KB
 constexpr int kStageBytes = 2 * kTileBytes;    // K + V
 constexpr int kRing = kNW * kNS * kStageBytes;
-constexpr int kSmem = kRing + kNW * kNS * 8 + 1024;  // + barriers + slack for 1024 alignment
+constexpr int kSmem = kRing + kNW * kNS * 8 + 16 + 1024;  // + barriers + last-CTA flag + slack for 1024 alignment
 constexpr float kRescaleAt = 8.0f;             // log2 units
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -332,6 +333,8 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
             }
         }
     }
+    if (p.counters && rm.n_split > 1)
+        finish_split_row(p, item.row, h, rm.n_split, G, kD, reinterpret_cast<int*>(smem + kRing + kNW * kNS * 8));
 }
 
 bool decode_mma_supported(int dtype, int D, int G, int block_size) {

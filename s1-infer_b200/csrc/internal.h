@@ -93,6 +93,8 @@ struct AttnParams {
     int32_t layer;
     float scale_log2;      // log2(e) / sqrt(D)
     int* err;
+    int32_t* counters;     // [n_rows][Hkv] arrivals of split CTAs, zero between launches;
+                           // NULL = partials are merged by a separate combine launch
 };
 
 // One sequence of a prefill batch (tensor-core prefill kernel).
@@ -235,6 +237,7 @@ struct s1kv_pool {
     // device helpers
     s1kv::Stager stager;
     s1kv::DevBuf scratch;             // split-K partials
+    s1kv::DevBuf counters;            // split-K arrival counters (kept at zero)
     s1kv::DevBuf io;                  // host-pointer step buffers
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t io_ev[4] = {nullptr, nullptr, nullptr, nullptr};

@@ -465,6 +465,7 @@ int s1kv_pool_destroy(s1kv_pool* p) {
         cudaDeviceSynchronize();
         p->stager.destroy();
         p->scratch.destroy();
+        p->counters.destroy();
         p->io.destroy();
         if (p->k) cudaFree(p->k);
         if (p->v) cudaFree(p->v);
