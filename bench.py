@@ -512,6 +512,90 @@ def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3):
             "attn_bytes_per_layer_per_gpu": attn_bytes, "kv_gbs_per_gpu": attn_bytes / (attn_ms * 1e-3) / 1e9}
 
 
+def run_cfg5(s1kv, torch, rank, world, steps=100, warmup=20):
+    """cfg5, pool churn, one GPU's share of a sequence-sharded 8-GPU box
+    (512 running sequences, 8 arrivals per step, 55k blocks per layer):
+    64 running sequences on a pool of 6875 blocks per layer (32 layers,
+    Hq 32 / Hkv 8 / D 128, bf16), Poisson(1) arrivals per step, prompts
+    log-normal (median 1024, sigma 0.8), outputs U[32, 512], 30% of the
+    prompts starting with one of 16 prefixes of U[256, 4096] tokens, LRU
+    eviction of zero-refcount prefix blocks (s1kv.churn; seed 4, and
+    1000 * rank added per rank).  A step: retire finished requests, admit
+    queued ones (prefix-cache match, reserve, prompt K/V appended),
+    one-token RoPE + append for every running sequence and decode attention
+    over its blocks, all 32 layers.  Timed on the wall clock (host
+    bookkeeping included) and with CUDA events."""
+    from s1kv.churn import ChurnDriver, ChurnWorkload
+    layers, max_blocks, max_running = 32, 55000 // 8, 64
+    order = np.random.default_rng(4 + rank).permutation(max_blocks).astype(np.int32)
+    pool = s1kv.Pool(layers, HKV, D, max_blocks, BS, dtype="bf16", initial_free_list=order,
+                     max_seqs=4 * max_running)
+    wl = ChurnWorkload(seed=4 + 1000 * rank)
+    drv = ChurnDriver(pool, wl, max_running=max_running)
+    drv.queue.extend(wl.request() for _ in range(max_running))
+    gen = torch.Generator(device="cuda").manual_seed(41 + rank)
+    cap = 1 << 17
+    kbuf = torch.randn((cap, HKV, D), device="cuda", generator=gen)
+    vbuf = torch.randn((cap, HKV, D), device="cuda", generator=gen)
+    qbuf = torch.randn((max_running, HQ, D), device="cuda", generator=gen)
+    host = [0.0]
+
+    def step():
+        h0 = time.perf_counter()
+        plan = drv.plan()
+        b = drv.open(plan)
+        host[0] += time.perf_counter() - h0
+        assert plan.n_tokens <= cap
+        for layer in range(layers):
+            q = qbuf[:plan.n_rows] if plan.n_rows else None
+            qr = b.rope_append(layer, kbuf[:plan.n_tokens], vbuf[:plan.n_tokens], q=q)
+            if plan.n_rows:
+                b.attention(layer, qr)
+        h0 = time.perf_counter()
+        b.end()
+        drv.close(plan)
+        host[0] += time.perf_counter() - h0
+
+    step()
+    rng = np.random.default_rng(7 + rank)
+    for s in drv.running:  # steady state: the first requests are somewhere inside their outputs
+        drv.running[s] = int(rng.integers(1, drv.running[s] + 1))
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(torch, world)
+    s0 = dict(drv.stats)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    host[0] = 0.0
+    t0 = time.perf_counter()
+    ev0.record()
+    for _ in range(steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    wall_ms = (time.perf_counter() - t0) * 1e3
+    gpu_ms = ev0.elapsed_time(ev1)
+    d = {k: drv.stats[k] - s0.get(k, 0) for k in drv.stats}
+    st = pool.stats()
+    assert pool.check_device() == 0
+    pool.close()
+    del kbuf, vbuf, qbuf
+    torch.cuda.empty_cache()
+    wall_max = max_over_ranks(torch, world, wall_ms)
+    dec = sum_over_ranks(torch, world, float(d.get("decode_tokens", 0)))
+    app = sum_over_ranks(torch, world, float(d.get("appended_tokens", 0)))
+    return {"workload": "cfg5 per GPU: 64 running seqs, Poisson(1) arrivals, prompts lognormal(1024, 0.8), outputs "
+                        "U[32,512], 30% reuse of 16 prefixes U[256,4096], LRU eviction, pool 6875 blocks x 32 "
+                        "layers bf16 Hq32/Hkv8/D128 (seed 4)",
+            "parallelism": f"sequence-sharded x{world}, independent pools, no collective", "scaling": "weak",
+            "steps": steps, "decode_tok_s": dec / (wall_max * 1e-3), "appended_tok_s": app / (wall_max * 1e-3),
+            "ms_per_step": wall_max / steps, "gpu_ms_per_step": gpu_ms / steps,
+            "host_bookkeeping_ms_per_step": host[0] * 1e3 / steps,
+            "per_gpu_in_window": {k: d.get(k, 0) for k in ("admitted", "retired", "deferred", "preempted",
+                                                             "prefix_hit_tokens", "decode_tokens", "appended_tokens")},
+            "evictions_total": st["evictions"], "occupancy": 1.0 - st["num_free"] / max_blocks}
+
+
 def run_ours(args):
     import torch
     import s1kv
@@ -534,10 +618,11 @@ def run_ours(args):
                                  timed_e2e=not args.no_e2e, sample_clocks=(dtype == "f32"))
     cfg3 = run_cfg3(s1kv, torch, rank, n=args.cfg3_seqs) if not args.only or args.only == "cfg3" else None
     cfg4 = run_cfg4(s1kv, torch, rank, world) if not args.only or args.only == "cfg4" else None
+    cfg5 = run_cfg5(s1kv, torch, rank, world) if not args.only or args.only == "cfg5" else None
     if args.only:
         # profiling case: one variant, no summary line
-        if rank == 0 and args.only in ("cfg3", "cfg4"):
-            print(json.dumps({"profiling_case": args.only, **(cfg3 if args.only == "cfg3" else cfg4)}))
+        if rank == 0 and args.only in ("cfg3", "cfg4", "cfg5"):
+            print(json.dumps({"profiling_case": args.only, **{"cfg3": cfg3, "cfg4": cfg4, "cfg5": cfg5}[args.only]}))
         elif rank == 0:
             r = res[args.only]
             print(json.dumps({"profiling_case": args.only, "layers": LAYERS, "ms_per_step": r["elapsed_ms"] / args.steps,
@@ -616,7 +701,8 @@ def run_ours(args):
                 "decode_ms_per_step_per_layer": cfg3["decode_ms_per_step"]},
             "cfg4_head_sharded": None if cfg4 is None else {
                 **cfg4, "roofline": {"bound": "hbm", "achieved": cfg4["kv_gbs_per_gpu"], "peak": peak,
-                                     "frac": cfg4["kv_gbs_per_gpu"] / peak, "unit": "GB/s"}}},
+                                     "frac": cfg4["kv_gbs_per_gpu"] / peak, "unit": "GB/s"}},
+            "cfg5_churn": cfg5},
         "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
     }
     print(json.dumps(line))
@@ -683,7 +769,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling cases only (the bench line uses 32)")
-    ap.add_argument("--only", choices=["f32", "bf16", "cfg3", "cfg4"], help="profiling case: run one variant")
+    ap.add_argument("--only", choices=["f32", "bf16", "cfg3", "cfg4", "cfg5"], help="profiling case: run one variant")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cfg3-seqs", type=int, default=256, help="profiling case: sequences of the cfg3 variant")
     args = ap.parse_args()

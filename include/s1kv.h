@@ -282,8 +282,10 @@ int s1kv_batch_begin(s1kv_pool* pool, const uint64_t* seqs, const int32_t* n_app
 /* Total appended tokens and query rows of the batch. */
 int s1kv_batch_sizes(const s1kv_batch* batch, int64_t* n_tokens, int64_t* n_rows);
 /* RoPE + append of this step's k, v [n_tokens][num_kv_heads][head_dim]; q
- * [n_rows][n_q_heads][head_dim] rotated into q_out when q_in is non-NULL
- * (n_rows must equal n_tokens then). */
+ * [n_rows][n_q_heads][head_dim] rotated into q_out when q_in is non-NULL,
+ * each query row at its own position (the last q_len positions of its
+ * sequence), so a step may mix prompts appended without queries and
+ * decode rows. */
 int s1kv_batch_rope_append(s1kv_batch* batch, int32_t layer, const float* q_in, float* q_out, int32_t n_q_heads,
                            const float* k, const float* v, void* stream);
 /* Append without RoPE (KVBlockPool::append data movement). */

@@ -132,6 +132,7 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
                              (long long)lens[i]);
         }
         if (ql != 1 && ql != 0) b->decode_rows = false;
+        if (ql != (n_append ? n_append[i] : 0)) b->rows_are_tokens = false;
         n_rows += ql;
     }
     b->rows.resize(n_rows);
@@ -191,7 +192,8 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
     // One upload of the step's metadata.
     size_t o_slots = 0, o_pos = align16(o_slots + n_tok * 4), o_rows = align16(o_pos + n_tok * 4),
            o_items = align16(o_rows + n_rows * sizeof(RowMeta)), o_pseq = align16(o_items + items.size() * sizeof(WorkItem)),
-           total = align16(o_pseq + pseqs.size() * sizeof(PrefillSeq));
+           o_qpos = align16(o_pseq + pseqs.size() * sizeof(PrefillSeq)),
+           total = align16(o_qpos + (b->rows_are_tokens ? 0 : n_rows * 4));
     st = p->stager.acquire(total + 16, &b->seg);
     if (st) {
         delete b;
@@ -203,12 +205,17 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
     std::memcpy(h + o_rows, b->rows.data(), n_rows * sizeof(RowMeta));
     std::memcpy(h + o_items, items.data(), items.size() * sizeof(WorkItem));
     std::memcpy(h + o_pseq, pseqs.data(), pseqs.size() * sizeof(PrefillSeq));
+    if (!b->rows_are_tokens) {
+        int32_t* qp = reinterpret_cast<int32_t*>(h + o_qpos);
+        for (int64_t r = 0; r < n_rows; r++) qp[r] = b->rows[r].kv_len - 1;
+    }
     if (total) S1KV_CUDA(cudaMemcpyAsync(b->seg->d, h, total, cudaMemcpyHostToDevice, stream));
     b->d_slots = (const int32_t*)(b->seg->d + o_slots);
     b->d_pos = (const int32_t*)(b->seg->d + o_pos);
     b->d_rows = (const RowMeta*)(b->seg->d + o_rows);
     b->d_items = (const WorkItem*)(b->seg->d + o_items);
     b->d_pseqs = (const PrefillSeq*)(b->seg->d + o_pseq);
+    b->d_qpos = b->rows_are_tokens ? nullptr : (const int32_t*)(b->seg->d + o_qpos);
     *out = b;
     return S1KV_OK;
 }
@@ -232,15 +239,19 @@ static int batch_append_impl(s1kv_batch* b, int32_t layer, const float* q_in, fl
     s1kv_pool* p = b->pool;
     int st = check_layer(p, layer);
     if (st) return st;
-    if (b->n_tokens == 0) return S1KV_OK;
+    if (b->n_tokens == 0 && !(rope && q_in && b->n_rows)) return S1KV_OK;
     S1KV_ON_DEVICE(p->device);
-    if (!k || !v) return set_error(S1KV_EINVAL, "s1kv_batch_append: null k/v");
-    if (q_in && (!q_out || Hq <= 0 || b->n_rows != b->n_tokens))
-        return set_error(S1KV_EINVAL, "s1kv_batch_rope_append: q needs q_out, n_q_heads and one row per token");
+    if (b->n_tokens && (!k || !v)) return set_error(S1KV_EINVAL, "s1kv_batch_append: null k/v");
+    if (q_in && (!q_out || Hq <= 0))
+        return set_error(S1KV_EINVAL, "s1kv_batch_rope_append: q needs q_out and n_q_heads");
+    // Query rows that are exactly the appended tokens rotate in the append
+    // kernel; otherwise (a step mixing prompt appends without queries and
+    // decode rows) q is rotated by row position in a second launch.
+    const bool fused_q = rope && q_in && b->rows_are_tokens;
     AppendParams ap{};
     ap.k = k;
     ap.v = v;
-    ap.q_in = rope ? q_in : nullptr;
+    ap.q_in = fused_q ? q_in : nullptr;
     ap.q_out = q_out;
     ap.slots = b->d_slots;
     ap.pos = b->d_pos;
@@ -257,7 +268,14 @@ static int batch_append_impl(s1kv_batch* b, int32_t layer, const float* q_in, fl
                              &ap.rope_cap, stream, &st);
         if (st) return st;
     }
-    return launch_append(ap, p->desc.dtype, rope, stream);
+    if (b->n_tokens) {
+        st = launch_append(ap, p->desc.dtype, rope, stream);
+        if (st) return st;
+    }
+    if (rope && q_in && !fused_q && b->n_rows)
+        return launch_rope(q_in, q_out, ap.rope, ap.rope_cap, 0, b->n_rows, Hq, p->desc.head_dim, p->d_err, stream,
+                           b->d_qpos);
+    return S1KV_OK;
 }
 
 int s1kv_batch_rope_append(s1kv_batch* b, int32_t layer, const float* q_in, float* q_out, int32_t Hq, const float* k,

@@ -253,6 +253,8 @@ struct s1kv_batch {
     int32_t split_tokens = 0;
     int64_t max_pos = 0;      // largest position appended + 1
     bool decode_rows = true;  // every row has q_len 1 for its sequence
+    bool rows_are_tokens = true;  // q_len == n_append for every sequence: query row i is appended token i
+    const int32_t* d_qpos = nullptr;  // position of each query row (kv_len - 1), when rows are not the tokens
     // device views into seg->d
     const int32_t* d_slots = nullptr;
     const int32_t* d_pos = nullptr;
@@ -270,8 +272,10 @@ namespace s1kv {
 int launch_table_update(const TableUpdate* d_upd, int64_t n, int32_t* table, int32_t max_bps, cudaStream_t stream);
 int launch_cow(s1kv_pool* pool, const int32_t* d_src, const int32_t* d_dst, int64_t n, cudaStream_t stream);
 int launch_append(const AppendParams& p, int dtype, bool rope, cudaStream_t stream);
+// Rotates n rows of H heads: row i at position pos[i], or start_pos + i
+// when pos is NULL.
 int launch_rope(const float* x, float* out, const float2* table, int64_t table_cap, int64_t start_pos, int64_t n,
-                int32_t H, int32_t D, int* err, cudaStream_t stream);
+                int32_t H, int32_t D, int* err, cudaStream_t stream, const int32_t* pos = nullptr);
 int launch_gather(s1kv_pool* pool, int32_t layer, int32_t row, int64_t len, int which, float* out,
                   cudaStream_t stream);
 // Paged attention over a prepared work list; picks the TMA split-K decode

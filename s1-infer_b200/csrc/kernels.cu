@@ -267,13 +267,14 @@ int launch_append(const AppendParams& p, int dtype, bool rope, cudaStream_t stre
 
 // ------------------------------------------------------- standalone RoPE --
 __global__ void rope_kernel(const float* __restrict__ x, float* __restrict__ out, const float2* __restrict__ tab,
-                            int64_t cap, int64_t start_pos, int64_t n, int H, int D, int* err) {
+                            int64_t cap, int64_t start_pos, const int32_t* __restrict__ pos_of, int64_t n, int H, int D,
+                            int* err) {
     const int half = D / 2;
     const int64_t total = n * H * half;
     for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
         int j = (int)(u % half);
         int64_t th = u / half;
-        int64_t pos = start_pos + th / H;
+        int64_t pos = pos_of ? (int64_t)pos_of[th / H] : start_pos + th / H;
         if (pos >= cap) {
             flag_error(err, kErrBounds);
             continue;
@@ -286,11 +287,11 @@ __global__ void rope_kernel(const float* __restrict__ x, float* __restrict__ out
 }
 
 int launch_rope(const float* x, float* out, const float2* table, int64_t cap, int64_t start_pos, int64_t n, int32_t H,
-                int32_t D, int* err, cudaStream_t stream) {
+                int32_t D, int* err, cudaStream_t stream, const int32_t* pos) {
     int64_t total = n * H * (D / 2);
     if (total <= 0) return S1KV_OK;
     int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, kSMs * 16));
-    rope_kernel<<<grid, 256, 0, stream>>>(x, out, table, cap, start_pos, n, H, D, err);
+    rope_kernel<<<grid, 256, 0, stream>>>(x, out, table, cap, start_pos, pos, n, H, D, err);
     g_launches++;
     S1KV_CUDA(cudaGetLastError());
     return S1KV_OK;
