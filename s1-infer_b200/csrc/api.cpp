@@ -304,7 +304,9 @@ int s1kv_batch_attention(s1kv_batch* b, int32_t layer, const float* q, float* ou
     // Chunks of several query rows per sequence over bf16 K/V are a dense
     // contraction: tensor-core prefill.  Decode rows stay on the split-K
     // kernel.
-    if (!b->decode_rows && p->tmap_sw_ok && prefill_tc_supported(p->desc.dtype, D, G, p->desc.block_size)) {
+    // (q and out are read and written by TMA there: 16-byte aligned.)
+    if (!b->decode_rows && p->tmap_sw_ok && prefill_tc_supported(p->desc.dtype, D, G, p->desc.block_size) &&
+        (((uintptr_t)q | (uintptr_t)out) & 15) == 0) {
         PrefillParams pp{};
         pp.q = q;
         pp.out = out;
@@ -318,6 +320,7 @@ int s1kv_batch_attention(s1kv_batch* b, int32_t layer, const float* q, float* ou
         pp.Hkv = Hkv;
         pp.layer = layer;
         pp.scale_log2 = scale_log2(D);
+        pp.n_rows = b->n_rows;
         pp.err = p->d_err;
         if (pp.n_seqs == 0 || pp.max_chunks == 0) return S1KV_OK;
         return launch_prefill_tc(pp, p->tmap_k_sw, p->tmap_v_sw, stream);

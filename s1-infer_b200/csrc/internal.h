@@ -117,6 +117,7 @@ struct PrefillParams {
     int32_t Hq, Hkv;
     int32_t layer;
     float scale_log2;
+    int64_t n_rows;          // rows of q / out (tensor-map extent)
     int* err;
 };
 

@@ -9,8 +9,11 @@
 //     M = 128 accumulator rows of a tile are (query, head) pairs: 128/G
 //     queries x the G query heads that share the KV head, so every K/V tile
 //     feeds all heads of the group, and both tiles share each K/V tile.
-//   * Q (fp32 in global) is narrowed to bf16 into shared memory in the
-//     128-byte-swizzled K-major layout UMMA reads.
+//   * Q (fp32 in global) arrives by TMA, one 128-row box per tile, in the
+//     K/V ring before its first use, and is narrowed to bf16 in the
+//     128-byte-swizzled K-major layout UMMA reads (rows query-major: row r =
+//     query r / G, head r % G).  Finished rows of full chunks leave through
+//     swizzled staging and TMA stores; partial chunks store directly.
 //   * K/V tiles of 128 tokens = 8 blocks come through the block table by
 //     TMA (one 16-row x 64-element box per block and 128-byte half of a
 //     row, 128B swizzle, no multicast), issued by 16 lanes of the producer
@@ -62,8 +65,12 @@ constexpr int kOffQ = 0;                        // Q_A, Q_B
 constexpr int kOffK = kOffQ + 2 * kQBytes;      // K ring
 constexpr int kOffV = kOffK + kStages * kKBytes;  // V ring
 constexpr int kOffBar = kOffV + kStages * kVBytes;
-// barriers: k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], pv_done[2], drain
-constexpr int kNumBars = 4 * kStages + 7;
+// barriers: k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], pv_done[2], drain, q_full
+constexpr int kNumBars = 4 * kStages + 8;
+// Q arrives as fp32 by TMA into the (still idle) K/V ring: one box of
+// 128 (query, head) rows x 512 bytes per query tile
+constexpr int kQStageBytes = kM * kD * 4;
+static_assert(2 * kQStageBytes == kStages * (kKBytes + kVBytes), "Q staging must fill the K/V ring exactly");
 constexpr int kOffMisc = kOffBar + kNumBars * 8;  // tmem slot, abort flag
 constexpr int kIdsCached = 256;                   // block ids of the first 32 tiles (4096 tokens)
 constexpr int kOffIds = (kOffMisc + 16 + 15) / 16 * 16;
@@ -100,6 +107,19 @@ __device__ __forceinline__ void tma4(void* dst, const CUtensorMap* m, uint64_t* 
         "[%6];" ::"r"(su32(dst)),
         "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(su32(b))
         : "memory");
+}
+
+__device__ __forceinline__ void tma3_load(void* dst, const CUtensorMap* m, uint64_t* b, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+            su32(dst)),
+        "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(su32(b))
+        : "memory");
+}
+__device__ __forceinline__ void tma3_store(const CUtensorMap* m, uint32_t src, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(m), "r"(c0),
+                 "r"(c1), "r"(c2), "r"(src)
+                 : "memory");
 }
 
 // UMMA shared-memory descriptor, 128-byte swizzle (layout type 2), version 1.
@@ -204,10 +224,6 @@ __device__ __forceinline__ void tmem_st16_nowait(uint32_t taddr, const float* v)
         "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
         : "memory");
 }
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
-    tmem_st32_nowait(taddr, v);
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
 
 __device__ __forceinline__ float ex2f(float x) {
     float y;
@@ -247,7 +263,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t phase, volatile 
 template <int G>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant__ CUtensorMap tmK,
-                      const __grid_constant__ CUtensorMap tmV) {
+                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQ,
+                      const __grid_constant__ CUtensorMap tmO) {
     constexpr int QT = kM / G;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -260,6 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* p_full = bars + 4 * kStages + 2;   // [2]
     uint64_t* pv_done = bars + 4 * kStages + 4;  // [2]
     uint64_t* drain = bars + 4 * kStages + 6;
+    uint64_t* q_full = bars + 4 * kStages + 7;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
     int32_t* sIds = reinterpret_cast<int32_t*>(smem + kOffIds);
@@ -284,10 +302,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (tid == 0) {
         for (int i = 0; i < kNumBars; i++) bar_init(&bars[i], 1);
-        bar_init(&p_full[0], 128);
-        bar_init(&p_full[1], 128);
+        bar_init(&p_full[0], 4);  // one arrive per softmax warp
+        bar_init(&p_full[1], 4);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        // both query tiles, fp32, rows (query, head) query-major; rows past
+        // the end of q read as zeros
+        bar_expect(q_full, 2 * kQStageBytes);
+        for (int X = 0; X < 2; X++)
+            tma3_load(smem + kOffK + X * kQStageBytes, &tmQ, q_full, 0, h * G, sm.q_start + q0 + X * QT);
     }
     auto lookup = [&](int i) -> int32_t {
         if (i * 16 >= sm.kv_len) return p.max_blocks;  // past the end: zero-filled box
@@ -299,22 +322,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         return blk;
     };
     for (int i = tid; i < min(n_tiles * kBlocksPerTile, kIdsCached); i += kThreads) sIds[i] = lookup(i);
-    // Q tiles (softmax threads): row r of tile X is head r / QT, query X*QT + r % QT.
-    if (tid < kSoftmaxThreads) {
-        const int X = tid >> 7, r = tid & 127;
-        const int g = r / QT, qi = X * QT + r % QT;
-        const bool valid = q0 + qi < sm.q_len;
-        const float* qrow = p.q + ((int64_t)(sm.q_start + (valid ? q0 + qi : 0)) * p.Hq + h * G + g) * kD;
-        uint8_t* sQ = smem + kOffQ + X * kQBytes;
-#pragma unroll 4
-        for (int c = 0; c < 16; c++) {
-            float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-            if (valid) {
-                a = __ldg(reinterpret_cast<const float4*>(qrow + c * 8));
-                b = __ldg(reinterpret_cast<const float4*>(qrow + c * 8 + 4));
-            }
-            uint4 w = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y), pack_bf16(b.z, b.w));
-            *reinterpret_cast<uint4*>(sQ + (c >> 3) * (kM * 128) + swz(r, c & 7)) = w;
+    // Q tiles: row r of tile X is query X*QT + r / G, head r % G.  Each
+    // softmax warp narrows rows w, w + 8, ... from the fp32 staging (one
+    // 512-byte row per warp access) to bf16 in the 128B-swizzled layout.
+    __syncthreads();  // barrier initialisation visible before anyone waits
+    if (tid < kSoftmaxThreads && warp_wait(q_full, 0, abort_flag)) {
+        const uint8_t* stage = smem + kOffK;
+        for (int R = warp; R < 2 * kM; R += kSoftmaxThreads / 32) {
+            const int X = R >> 7, r = R & (kM - 1);
+            const float4 a = *reinterpret_cast<const float4*>(stage + X * kQStageBytes + r * 512 + lane * 16);
+            *reinterpret_cast<uint2*>(smem + kOffQ + X * kQBytes + (lane >> 4) * (kM * 128) + swz(r, (lane & 15) >> 1) +
+                                      (lane & 1) * 8) = make_uint2(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w));
         }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -415,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ================= softmax warpgroups =================
         const int X = tid >> 7, r = tid & 127;
-        const int g = r / QT, qi = X * QT + r % QT;
+        const int g = r % G, qi = X * QT + r / G;
         const bool valid = q0 + qi < sm.q_len;
         const int row_limit = prefix + q0 + qi;  // last visible token
         const uint32_t lane_base = (uint32_t)(32 * ((tid >> 5) & 3)) << 16;
@@ -484,22 +502,57 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             l += (ls2[0].x + ls2[1].x) + (ls2[0].y + ls2[1].y);
             tc_fence_before();
-            bar_arrive(&p_full[X]);
+            __syncwarp();
+            if (lane == 0) bar_arrive(&p_full[X]);
         }
-        // last PV of this tile, then the output row
+        // last PV of this tile, then the output rows
         if (ok && warp_wait(&pv_done[X], (uint32_t)((n_tiles - 1) & 1), abort_flag)) {
             tc_fence_after();
             const float inv = 1.0f / l;
-            float* orow = p.out + ((int64_t)(sm.q_start + q0 + qi) * p.Hq + h * G + g) * kD;
+            if (q0 + 2 * QT <= sm.q_len) {
+                // Full chunk: this warp's 32 rows (times 1/l) go through
+                // 128B-swizzled staging (row r at r * 128 bytes of each
+                // 32-float column block) and four TMA stores of {32 floats,
+                // G heads, 32 / G queries}.  Every MMA that reads the staging
+                // is done: tile A uses the Q buffers (their last reader, S_B,
+                // was issued before PV_A), tile B the K/V ring (after the last
+                // MMA).  The staging address is recomputed here from the
+                // shared-memory symbol and stored through st.shared: a generic
+                // pointer kept from the prologue costs the main loop spills.
+                const uint32_t stage = ((su32(smem_raw) + 1023u) & ~1023u) + (X == 0 ? kOffQ : kOffK);
 #pragma unroll 1
-            for (int c = 0; c < kD / 32; c++) {
-                float ov[32];
-                tmem_ld32(tO + c * 32, ov);
-                if (valid) {
+                for (int a = 0; a < kD / 32; a++) {
+                    float ov[32];
+                    tmem_ld32(tO + a * 32, ov);
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4)
-                        *reinterpret_cast<float4*>(orow + c * 32 + j) =
-                            make_float4(ov[j] * inv, ov[j + 1] * inv, ov[j + 2] * inv, ov[j + 3] * inv);
+                    for (int c = 0; c < 8; c++)
+                        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(stage + a * (kM * 128) + swz(r, c)),
+                                     "f"(ov[4 * c] * inv), "f"(ov[4 * c + 1] * inv), "f"(ov[4 * c + 2] * inv),
+                                     "f"(ov[4 * c + 3] * inv)
+                                     : "memory");
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    const int wr = 32 * (warp & 3);  // first row of this warp
+                    for (int a = 0; a < kD / 32; a++)
+                        tma3_store(&tmO, stage + a * (kM * 128) + wr * 128, a * 32, h * G, sm.q_start + q0 + X * QT + wr / G);
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                }
+                __syncwarp();
+            } else {
+                float* orow = p.out + ((int64_t)(sm.q_start + q0 + qi) * p.Hq + h * G + g) * kD;
+#pragma unroll 1
+                for (int c = 0; c < kD / 32; c++) {
+                    float ov[32];
+                    tmem_ld32(tO + c * 32, ov);
+                    if (valid) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4*>(orow + c * 32 + j) =
+                                make_float4(ov[j] * inv, ov[j + 1] * inv, ov[j + 2] * inv, ov[j + 3] * inv);
+                    }
                 }
             }
         }
@@ -508,7 +561,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- tear-down: every path frees TMEM ----
     tc_fence_before();
     __syncthreads();
-    if (tid == 0 && *abort_flag) atomicOr(p.err, kErrTimeout);
+    if (tid == 0 && *abort_flag) {
+        atomicOr(p.err, kErrTimeout);
+        bar_wait(q_full, 0);  // the Q copy has landed before the CTA exits (bounded)
+    }
     if (warp == 0) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
@@ -523,11 +579,41 @@ bool prefill_tc_supported(int dtype, int D, int G, int block_size) {
     return dtype == S1KV_DTYPE_BF16 && D == kD && block_size == 16 && (G == 1 || G == 2 || G == 4 || G == 8);
 }
 
+// Tensor maps over this call's q and out ([n_rows][Hq][128] fp32): q is
+// read one query tile (128 rows of (query, head)) per box; out is written
+// in 128B-swizzled boxes of {32 floats, G heads, 32 / G queries}.
+static int encode_q_out_maps(const PrefillParams& p, int G, CUtensorMap* tq, CUtensorMap* to) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        S1KV_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !fn) return set_error(S1KV_ECUDA, "s1kv: cuTensorMapEncodeTiled unavailable");
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)p.Hq, (cuuint64_t)p.n_rows};
+    cuuint64_t strides[2] = {(cuuint64_t)kD * 4, (cuuint64_t)p.Hq * kD * 4};
+    cuuint32_t estr[3] = {1, 1, 1};
+    cuuint32_t box_q[3] = {(cuuint32_t)kD, (cuuint32_t)G, (cuuint32_t)(kM / G)};
+    CUresult r = encode(tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(p.q), dims, strides, box_q, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(S1KV_EINVAL, "prefill: tensor map over q rejected (%d)", (int)r);
+    cuuint32_t box_o[3] = {32, (cuuint32_t)G, (cuuint32_t)(32 / G)};
+    r = encode(to, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, p.out, dims, strides, box_o, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(S1KV_EINVAL, "prefill: tensor map over out rejected (%d)", (int)r);
+    return S1KV_OK;
+}
+
 template <int G>
 static int launch_prefill_g(const PrefillParams& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream) {
+    CUtensorMap tq, to;
+    int st = encode_q_out_maps(p, G, &tq, &to);
+    if (st) return st;
     S1KV_CUDA(cudaFuncSetAttribute(prefill_tc_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
     dim3 grid((unsigned)(p.n_seqs * p.max_chunks), (unsigned)p.Hkv);
-    prefill_tc_kernel<G><<<grid, kThreads, kSmem, stream>>>(p, tk, tv);
+    prefill_tc_kernel<G><<<grid, kThreads, kSmem, stream>>>(p, tk, tv, tq, to);
     g_launches++;
     S1KV_CUDA(cudaGetLastError());
     return S1KV_OK;
