@@ -453,6 +453,17 @@ int s1kv_pool_create(const s1kv_pool_desc* d, int device, s1kv_pool** out) {
             s1kv_pool_destroy(p);
             return st;
         }
+        // The RoPE table is computed on the host (bit-exact cos/sin) and
+        // growing it synchronises the device, so it is built here for every
+        // position the pool can hold (up to 2^18), not in the middle of a
+        // decode loop when a sequence first crosses a power of two.
+        int64_t rope_cap = 0;
+        rope_table(device, d->head_dim, p->desc.rope_theta, std::min<int64_t>(p->desc.max_seq_len, int64_t(1) << 18),
+                   &rope_cap, nullptr, &st);
+        if (st) {
+            s1kv_pool_destroy(p);
+            return st;
+        }
     }
     *out = p;
     return S1KV_OK;
