@@ -52,6 +52,35 @@ int32_t plan_split_tiles(int64_t total_tiles, int32_t Hkv, int nw) {
 
 float scale_log2(int D) { return 1.4426950408889634f / std::sqrt((float)D); }
 
+// Split-K work list of a batch's query rows (host): split length, per-row
+// split count and partial offset, items longest first.
+void plan_items(const s1kv_pool* p, s1kv_batch* b) {
+    const int32_t bs = p->desc.block_size;
+    const int nw = tma_warps_per_cta(p->desc.dtype, p->desc.head_dim);
+    int64_t total_tiles = 0;
+    for (const RowMeta& m : b->rows) total_tiles += (m.kv_len + bs - 1) / bs;
+    b->split_tokens = plan_split_tiles(total_tiles, p->desc.num_kv_heads, nw) * 16;
+    std::vector<WorkItem>& items = b->items;
+    items.clear();
+    int64_t n_part = 0;
+    for (int64_t r = 0; r < (int64_t)b->rows.size(); r++) {
+        RowMeta& m = b->rows[r];
+        m.n_split = (m.kv_len + b->split_tokens - 1) / b->split_tokens;
+        m.part_off = (int32_t)n_part;
+        if (m.n_split > 1) n_part += m.n_split;
+        for (int32_t s = 0; s < m.n_split; s++) items.push_back({(int32_t)r, s});
+    }
+    // Longest work first: full splits, then the tails by length.
+    auto item_tokens = [&](const WorkItem& w) {
+        return std::min<int64_t>(b->split_tokens, b->rows[w.row].kv_len - (int64_t)w.split * b->split_tokens);
+    };
+    std::stable_sort(items.begin(), items.end(),
+                     [&](const WorkItem& a, const WorkItem& c) { return item_tokens(a) > item_tokens(c); });
+    b->n_items = (int64_t)items.size();
+    b->n_part = n_part;
+    b->items_planned = true;
+}
+
 }  // namespace
 }  // namespace s1kv
 
@@ -136,9 +165,6 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
         n_rows += ql;
     }
     b->rows.resize(n_rows);
-    std::vector<WorkItem> items;
-    const int nw = tma_warps_per_cta(p->desc.dtype, p->desc.head_dim);
-    int64_t total_tiles = 0;
     {
         int64_t r = 0;
         for (int32_t i = 0; i < n_seqs; i++) {
@@ -147,29 +173,17 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
                 RowMeta& m = b->rows[r];
                 m.table_row = trow[i];
                 m.kv_len = (int32_t)(lens[i] - ql + j + 1);
-                total_tiles += (m.kv_len + bs - 1) / bs;
+                m.n_split = 1;
+                m.part_off = 0;
             }
         }
     }
-    const int32_t split_tiles = plan_split_tiles(total_tiles, p->desc.num_kv_heads, nw);
-    b->split_tokens = split_tiles * 16;
-    int64_t n_part = 0;
-    for (int64_t r = 0; r < n_rows; r++) {
-        RowMeta& m = b->rows[r];
-        m.n_split = (m.kv_len + b->split_tokens - 1) / b->split_tokens;
-        m.part_off = (int32_t)n_part;
-        if (m.n_split > 1) n_part += m.n_split;
-        for (int32_t s = 0; s < m.n_split; s++) items.push_back({(int32_t)r, s});
-    }
-    // Longest work first: full splits, then the tails by length.
-    auto item_tokens = [&](const WorkItem& w) {
-        return std::min<int64_t>(b->split_tokens, b->rows[w.row].kv_len - (int64_t)w.split * b->split_tokens);
-    };
-    std::stable_sort(items.begin(), items.end(),
-                     [&](const WorkItem& a, const WorkItem& c) { return item_tokens(a) > item_tokens(c); });
+    // Decode batches get their split-K work list now.  Query chunks take the
+    // tensor-core prefill, which does not use it; it is planned on demand if
+    // such a batch falls back to the split-K kernels.
+    if (b->decode_rows) plan_items(p, b);
+    const std::vector<WorkItem>& items = b->items;
     b->n_rows = n_rows;
-    b->n_items = (int64_t)items.size();
-    b->n_part = n_part;
     // Per-sequence view of the same rows, for the tensor-core prefill.
     std::vector<PrefillSeq> pseqs(n_seqs);
     {
@@ -214,6 +228,7 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
     b->d_pos = (const int32_t*)(b->seg->d + o_pos);
     b->d_rows = (const RowMeta*)(b->seg->d + o_rows);
     b->d_items = (const WorkItem*)(b->seg->d + o_items);
+    b->items_uploaded = b->items_planned;
     b->d_pseqs = (const PrefillSeq*)(b->seg->d + o_pseq);
     b->d_qpos = b->rows_are_tokens ? nullptr : (const int32_t*)(b->seg->d + o_qpos);
     *out = b;
@@ -229,6 +244,7 @@ int s1kv_batch_sizes(const s1kv_batch* b, int64_t* n_tokens, int64_t* n_rows) {
 
 int s1kv_batch_plan(const s1kv_batch* b, int32_t* split_tokens, int64_t* n_items) {
     if (!b) return set_error(S1KV_EINVAL, "null batch");
+    if (!b->items_planned) plan_items(b->pool, const_cast<s1kv_batch*>(b));
     if (split_tokens) *split_tokens = b->split_tokens;
     if (n_items) *n_items = b->n_items;
     return S1KV_OK;
@@ -324,6 +340,21 @@ int s1kv_batch_attention(s1kv_batch* b, int32_t layer, const float* q, float* ou
         pp.err = p->d_err;
         if (pp.n_seqs == 0 || pp.max_chunks == 0) return S1KV_OK;
         return launch_prefill_tc(pp, p->tmap_k_sw, p->tmap_v_sw, stream);
+    }
+    if (!b->items_uploaded) {
+        // A query-chunk batch on the split-K kernels (shapes or alignments the
+        // tensor-core prefill does not take): plan and upload its work list.
+        if (!b->items_planned) plan_items(p, b);
+        const size_t rb = b->rows.size() * sizeof(RowMeta), ib = b->items.size() * sizeof(WorkItem);
+        st = p->late_meta.ensure(align16(rb) + ib + 16);
+        if (st) return st;
+        char* d = (char*)p->late_meta.p;
+        S1KV_CUDA(cudaMemcpyAsync(d, b->rows.data(), rb, cudaMemcpyHostToDevice, stream));
+        S1KV_CUDA(cudaMemcpyAsync(d + align16(rb), b->items.data(), ib, cudaMemcpyHostToDevice, stream));
+        S1KV_CUDA(cudaStreamSynchronize(stream));  // the host vectors are pageable
+        b->d_rows = (const RowMeta*)d;
+        b->d_items = (const WorkItem*)(d + align16(rb));
+        b->items_uploaded = true;
     }
     size_t need = (size_t)b->n_part * Hkv * G * (D + 2) * sizeof(float);
     if (need) {

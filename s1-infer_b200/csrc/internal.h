@@ -239,6 +239,7 @@ struct s1kv_pool {
     s1kv::Stager stager;
     s1kv::DevBuf scratch;             // split-K partials
     s1kv::DevBuf counters;            // split-K arrival counters (kept at zero)
+    s1kv::DevBuf late_meta;           // rows + work list planned after batch_begin
     s1kv::DevBuf io;                  // host-pointer step buffers
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t io_ev[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -265,6 +266,9 @@ struct s1kv_batch {
     int32_t n_seqs = 0;
     int32_t max_qlen = 0;
     std::vector<s1kv::RowMeta> rows;  // host copy (for dispatch decisions)
+    std::vector<s1kv::WorkItem> items;  // split-K work list (host copy)
+    bool items_planned = false;       // rows' split fields and items computed
+    bool items_uploaded = false;      // d_rows / d_items carry them
 };
 
 namespace s1kv {

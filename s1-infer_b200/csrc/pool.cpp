@@ -477,6 +477,7 @@ int s1kv_pool_destroy(s1kv_pool* p) {
         p->stager.destroy();
         p->scratch.destroy();
         p->counters.destroy();
+        p->late_meta.destroy();
         p->io.destroy();
         if (p->k) cudaFree(p->k);
         if (p->v) cudaFree(p->v);
