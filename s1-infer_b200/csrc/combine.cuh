@@ -33,13 +33,67 @@ __device__ __forceinline__ void combine_partials(const AttnParams& p, int row, i
     }
 }
 
+// The same merge with the splits' (max, sum) staged in shared memory
+// (`sm`, at least 2 * (n_split + 1) * G floats): the maxima, weights and
+// normaliser are computed in parallel, then every (head, dim) output sums
+// its n_split partials with eight loads in flight.  Long rows (cfg4: 64+
+// splits per row) make the serial loop above latency-bound.
+__device__ __forceinline__ void combine_partials_staged(const AttnParams& p, int row, int h, int G, int D, float* sm) {
+    const RowMeta rm = p.rows[row];
+    const int ns = rm.n_split, tid = threadIdx.x, nt = blockDim.x;
+    float* w = sm;            // [ns][G]: max, then weight
+    float* ls = sm + ns * G;  // [ns][G]: sums
+    float* mg = ls + ns * G;  // [G]: global max, then 1 / normaliser
+    for (int i = tid; i < ns * G; i += nt) {
+        const int s = i / G, g = i % G;
+        const int64_t part = (int64_t)(rm.part_off + s) * p.Hkv + h;
+        w[i] = __ldcg(&p.part_ml[(part * G + g) * 2]);
+        ls[i] = __ldcg(&p.part_ml[(part * G + g) * 2 + 1]);
+    }
+    __syncthreads();
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int s = 0; s < ns; s++) M = fmaxf(M, w[s * G + tid]);
+        mg[tid] = M;
+    }
+    __syncthreads();
+    for (int i = tid; i < ns * G; i += nt) {
+        const float m = w[i];
+        float f = 0.0f;
+        if (m != -INFINITY) asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(f) : "f"(m - mg[i % G]));
+        w[i] = f;
+    }
+    __syncthreads();
+    if (tid < G) {
+        float L = 0.0f;
+        for (int s = 0; s < ns; s++) L = fmaf(ls[s * G + tid], w[s * G + tid], L);
+        mg[tid] = 1.0f / L;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < G * D; idx += nt) {
+        const int g = idx / D, d = idx % D;
+        const float* po = p.part_o + ((int64_t)rm.part_off * p.Hkv + h) * G * D + g * D + d;
+        const int64_t stride = (int64_t)p.Hkv * G * D;  // next split, same head
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        int s = 0;
+        for (; s + 8 <= ns; s += 8) {
+#pragma unroll
+            for (int u = 0; u < 8; u++) acc[u] = fmaf(__ldcg(po + (s + u) * stride), w[(s + u) * G + g], acc[u]);
+        }
+        for (; s < ns; s++) acc[0] = fmaf(__ldcg(po + s * stride), w[s * G + g], acc[0]);
+        const float O = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+        p.out[((int64_t)row * p.Hq + h * G + g) * D + d] = O * mg[g];
+    }
+}
+
 // Called by every CTA of a multi-split row once its partial is written:
 // the last CTA to arrive on the (row, head) counter merges the row and sets
 // the counter back to zero, so no separate combine launch is needed.
-// `flag` is one int of the caller's shared memory.  Every CTA arrives, also
-// after a timeout, so the counters always return to zero.
+// `flag` is one int of the caller's shared memory; `scratch` (free shared
+// memory of `scratch_floats` floats) stages the merge when it fits.  Every
+// CTA arrives, also after a timeout, so the counters always return to zero.
 __device__ __forceinline__ void finish_split_row(const AttnParams& p, int row, int h, int n_split, int G, int D,
-                                                 int* flag) {
+                                                 int* flag, float* scratch, int scratch_floats) {
     __threadfence();  // this CTA's partial is visible before its arrival
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -49,7 +103,10 @@ __device__ __forceinline__ void finish_split_row(const AttnParams& p, int row, i
     __syncthreads();
     if (*flag) {
         __threadfence();  // every other CTA's partial is visible to this one
-        combine_partials(p, row, h, G, D, threadIdx.x, blockDim.x);
+        if (2 * (n_split + 1) * G <= scratch_floats)
+            combine_partials_staged(p, row, h, G, D, scratch);
+        else
+            combine_partials(p, row, h, G, D, threadIdx.x, blockDim.x);
         if (threadIdx.x == 0) p.counters[(int64_t)row * p.Hkv + h] = 0;
     }
 }

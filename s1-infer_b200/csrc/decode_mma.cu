@@ -334,7 +334,8 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
         }
     }
     if (p.counters && rm.n_split > 1)
-        finish_split_row(p, item.row, h, rm.n_split, G, kD, reinterpret_cast<int*>(smem + kRing + kNW * kNS * 8));
+        finish_split_row(p, item.row, h, rm.n_split, G, kD, reinterpret_cast<int*>(smem + kRing + kNW * kNS * 8),
+                         reinterpret_cast<float*>(smem), kRing / 4);  // the rings are free by now
 }
 
 bool decode_mma_supported(int dtype, int D, int G, int block_size) {
