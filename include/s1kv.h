@@ -288,6 +288,16 @@ int s1kv_batch_sizes(const s1kv_batch* batch, int64_t* n_tokens, int64_t* n_rows
  * decode rows. */
 int s1kv_batch_rope_append(s1kv_batch* batch, int32_t layer, const float* q_in, float* q_out, int32_t n_q_heads,
                            const float* k, const float* v, void* stream);
+/* The same step from the raw projection outputs (src/nn/attention.cpp:
+ * 316-322): q [n_rows][n_q_heads][head_dim] and k [n_tokens][num_kv_heads]
+ * [head_dim] are RMS-normalised per head with q_norm_weight / k_norm_weight
+ * (device fp32 [head_dim]; src/nn/rmsnorm.cpp:4-33, bit-exact) and rotated;
+ * k and v go to their slots, q to q_out.  One kernel for rmsnorm(Q),
+ * rmsnorm(K), apply_rope(Q), apply_rope(K) and KVBlockPool::append.
+ * head_dim 64 or 128; pointers 16-byte aligned. */
+int s1kv_batch_norm_rope_append(s1kv_batch* batch, int32_t layer, const float* q_in, float* q_out, int32_t n_q_heads,
+                                const float* q_norm_weight, const float* k, const float* v, const float* k_norm_weight,
+                                float eps, void* stream);
 /* Append without RoPE (KVBlockPool::append data movement). */
 int s1kv_batch_append(s1kv_batch* batch, int32_t layer, const float* k, const float* v, void* stream);
 /* Paged GQA attention of the batch's query rows (post-RoPE q). */

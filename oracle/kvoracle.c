@@ -95,6 +95,19 @@ void kvo_apply_rope_pos(const float* x, int64_t T, int64_t H, int64_t D, const i
     for (int64_t i = 0; i < T; i++) rope_token(x + i * H * D, out + i * H * D, H, D, pos[i], base);
 }
 
+/* rmsnorm(input [rows, D], weight [D], eps) (src/nn/rmsnorm.cpp:4-33): per
+ * row, the squares summed in order, rms = sqrt(sum / D + eps), then
+ * (x / rms) * w. */
+void kvo_rmsnorm(const float* x, int64_t rows, int64_t D, const float* w, float eps, float* out) {
+    for (int64_t r = 0; r < rows; r++) {
+        const float* xr = x + r * D;
+        float sum = 0.0f;
+        for (int64_t j = 0; j < D; j++) sum += xr[j] * xr[j];
+        float rms = sqrtf(sum / (float)D + eps);
+        for (int64_t j = 0; j < D; j++) out[r * D + j] = (xr[j] / rms) * w[j];
+    }
+}
+
 /* The cos/sin pair the rotation uses for (pos, j), for table checks. */
 void kvo_rope_cs(int64_t pos, int64_t j, int64_t D, float base, float* c, float* s) {
     float theta = (float)pos / powf(base, (float)(2 * j) / (float)D);

@@ -59,6 +59,7 @@ def _load():
                 "kvo_apply_rope": (None, [vp, i64, i64, i64, i64, f32, vp]),
                 "kvo_apply_rope_pos": (None, [vp, i64, i64, i64, vp, f32, vp]),
                 "kvo_rope_cs": (None, [i64, i64, i64, f32, vp, vp]),
+                "kvo_rmsnorm": (None, [vp, i64, i64, vp, f32, vp]),
                 "kvo_gqa_attention": (None, [vp, vp, vp, i64, i64, i64, i64, i64, vp]),
                 "kvo_gqa_attention_paged": (None, [vp, i64, vp, vp, vp, i64, i64, i64, i64, i64, vp]),
                 "kvo_pool_new": (vp, [i64, i64, i64, i64]),
@@ -115,6 +116,7 @@ def _load_ref():
                 "ref_block_table": (C.c_int, [vp, u64, vp, i64, C.POINTER(i64)]),
                 "ref_pool_base": (C.POINTER(f32), [vp, u64, C.c_int]),
                 "ref_apply_rope": (None, [vp, i64, i64, i64, i64, vp]),
+                "ref_rmsnorm": (None, [vp, i64, i64, vp, f32, vp]),
                 "ref_gqa_attention": (None, [vp, vp, vp, i64, i64, i64, i64, i64, vp]),
                 "ref_gqa_attention_paged": (C.c_int, [vp, u64, vp, i64, i64, i64, i64, vp]),
                 "ref_decode_batch": (None, [vp, i64, vp, i64, vp, i64, i64, i64, i64, vp]),
@@ -158,6 +160,15 @@ def rope_table(max_pos, D, base=ROPE_BASE):
             lib.kvo_rope_cs(p, j, D, base, C.byref(c), C.byref(s))
             out[p, j, 0] = c.value
             out[p, j, 1] = s.value
+    return out
+
+
+def rmsnorm(x, w, eps=1e-6):
+    """rmsnorm over the last dim; src/nn/rmsnorm.cpp:4-33."""
+    lib = _load()
+    x, w = _f32(x), _f32(w)
+    out = np.empty_like(x)
+    lib.kvo_rmsnorm(_fp(x), x.size // x.shape[-1], x.shape[-1], _fp(w), eps, _fp(out))
     return out
 
 
@@ -378,6 +389,14 @@ def ref_apply_rope(x, start_pos=0):
         lib.ref_apply_rope(_fp(x), x.shape[0], x.shape[1], x.shape[2], start_pos, _fp(out))
     else:
         lib.ref_apply_rope(_fp(x), x.shape[0], 0, x.shape[1], start_pos, _fp(out))
+    return out
+
+
+def ref_rmsnorm(x, w, eps=1e-6):
+    lib = _load_ref()
+    x, w = _f32(x), _f32(w)
+    out = np.empty_like(x)
+    lib.ref_rmsnorm(_fp(x), x.size // x.shape[-1], x.shape[-1], _fp(w), eps, _fp(out))
     return out
 
 

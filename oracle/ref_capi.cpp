@@ -7,6 +7,7 @@
 // Wrapped reference entry points:
 //   KVBlockPool (include/infer/kv_block_pool.h:13-45)
 //   apply_rope (include/nn/RoPE.h:4)
+//   rmsnorm (include/nn/rmsnorm.h:4)
 //   GQA_attention / GQA_attention_paged (include/nn/attention.h:8-10)
 //   ThreadPool::parallel_for (include/infer/thread_pool.h:14)
 #include <cstdint>
@@ -19,6 +20,7 @@
 #include "infer/thread_pool.h"
 #include "nn/RoPE.h"
 #include "nn/attention.h"
+#include "nn/rmsnorm.h"
 
 namespace {
 
@@ -110,6 +112,10 @@ const float* ref_pool_base(void* p, uint64_t seq, int which) {
 void ref_apply_rope(const float* x, int64_t T, int64_t H, int64_t D, int64_t start_pos, float* out) {
     TensorPtr in = H > 0 ? make_tensor(x, {(size_t)T, (size_t)H, (size_t)D}) : make_tensor(x, {(size_t)T, (size_t)D});
     copy_out(apply_rope(in, (size_t)start_pos), out);
+}
+
+void ref_rmsnorm(const float* x, int64_t rows, int64_t D, const float* w, float eps, float* out) {
+    copy_out(rmsnorm(make_tensor(x, {(size_t)rows, (size_t)D}), make_tensor(w, {(size_t)D}), eps), out);
 }
 
 void ref_gqa_attention(const float* q, const float* k, const float* v, int64_t q_len, int64_t kv_len, int64_t Hq,

@@ -300,6 +300,47 @@ int s1kv_batch_rope_append(s1kv_batch* b, int32_t layer, const float* q_in, floa
     return batch_append_impl(b, layer, q_in, q_out, Hq, k, v, true, (cudaStream_t)stream);
 }
 
+int s1kv_batch_norm_rope_append(s1kv_batch* b, int32_t layer, const float* q_in, float* q_out, int32_t Hq,
+                                const float* q_norm_weight, const float* k, const float* v, const float* k_norm_weight,
+                                float eps, void* stream_) {
+    if (!b) return set_error(S1KV_EINVAL, "null batch");
+    s1kv_pool* p = b->pool;
+    int st = check_layer(p, layer);
+    if (st) return st;
+    const bool with_q = q_in && b->n_rows;
+    if (b->n_tokens == 0 && !with_q) return S1KV_OK;
+    S1KV_ON_DEVICE(p->device);
+    cudaStream_t stream = (cudaStream_t)stream_;
+    if (b->n_tokens && (!k || !v || !k_norm_weight))
+        return set_error(S1KV_EINVAL, "s1kv_batch_norm_rope_append: null k/v/k_norm_weight");
+    if (with_q && (!q_out || Hq <= 0 || !q_norm_weight))
+        return set_error(S1KV_EINVAL, "s1kv_batch_norm_rope_append: q needs q_out, n_q_heads and q_norm_weight");
+    if ((((uintptr_t)q_in | (uintptr_t)q_out | (uintptr_t)k | (uintptr_t)v) & 15) != 0)
+        return set_error(S1KV_EINVAL, "s1kv_batch_norm_rope_append: q/k/v must be 16-byte aligned");
+    AppendParams ap{};
+    ap.k = k;
+    ap.v = v;
+    ap.q_in = with_q ? q_in : nullptr;
+    ap.q_out = q_out;
+    ap.slots = b->d_slots;
+    ap.pos = b->d_pos;
+    ap.kpool = p->k + (size_t)layer * p->layer_bytes;
+    ap.vpool = p->v + (size_t)layer * p->layer_bytes;
+    ap.num_slots = p->num_slots;
+    ap.n = b->n_tokens;
+    ap.Hkv = p->desc.num_kv_heads;
+    ap.Hq = Hq;
+    ap.D = p->desc.head_dim;
+    ap.err = p->d_err;
+    ap.rope = rope_table(p->device, p->desc.head_dim, p->desc.rope_theta, std::max<int64_t>(b->max_pos, 1), &ap.rope_cap,
+                         stream, &st);
+    if (st) return st;
+    // query row i is token i unless the step mixes prompt appends without
+    // queries and decode rows; then each row has its own position
+    const int32_t* qpos = b->rows_are_tokens ? b->d_pos : b->d_qpos;
+    return launch_norm_rope_append(ap, p->desc.dtype, q_norm_weight, k_norm_weight, eps, qpos, b->n_rows, stream);
+}
+
 int s1kv_batch_append(s1kv_batch* b, int32_t layer, const float* k, const float* v, void* stream) {
     if (!b) return set_error(S1KV_EINVAL, "null batch");
     return batch_append_impl(b, layer, nullptr, nullptr, 0, k, v, false, (cudaStream_t)stream);

@@ -277,6 +277,9 @@ namespace s1kv {
 int launch_table_update(const TableUpdate* d_upd, int64_t n, int32_t* table, int32_t max_bps, cudaStream_t stream);
 int launch_cow(s1kv_pool* pool, const int32_t* d_src, const int32_t* d_dst, int64_t n, cudaStream_t stream);
 int launch_append(const AppendParams& p, int dtype, bool rope, cudaStream_t stream);
+// q/k RMSNorm + RoPE + append (k, v to slots; q rows at qpos to q_out).
+int launch_norm_rope_append(const AppendParams& p, int dtype, const float* qw, const float* kw, float eps,
+                            const int32_t* qpos, int64_t n_q_rows, cudaStream_t stream);
 // Rotates n rows of H heads: row i at position pos[i], or start_pos + i
 // when pos is NULL.
 int launch_rope(const float* x, float* out, const float2* table, int64_t table_cap, int64_t start_pos, int64_t n,

@@ -265,6 +265,100 @@ int launch_append(const AppendParams& p, int dtype, bool rope, cudaStream_t stre
     return S1KV_OK;
 }
 
+// ------------------------------------------- q/k RMSNorm + RoPE + append --
+// The projection outputs of one step straight into the cache
+// (src/nn/attention.cpp:316-322): q and k rows are RMS-normalised with their
+// weights (src/nn/rmsnorm.cpp:4-33: squares summed in order, sqrt(sum / D +
+// eps), x / rms * w, each operation rounded separately as in the reference's
+// build), rotated (RoPE), k written to its slot, q to q_out; v rows are
+// copied to their slots.  One thread per (token, head) row keeps the
+// reference's summation order, so the results are bit-exact.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) norm_rope_append_kernel(const AppendParams p, const float* __restrict__ qw,
+                                                               const float* __restrict__ kw, float eps,
+                                                               const int32_t* __restrict__ qpos, int64_t n_q_rows) {
+    constexpr int half = D / 2;
+    const int64_t q_units = p.q_in ? n_q_rows * p.Hq : 0;
+    const int64_t kv_units = p.n * p.Hkv;
+    const int64_t total = q_units + 2 * kv_units;
+    for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
+        int part;  // 0 = q, 1 = k, 2 = v
+        int64_t th;
+        if (u < q_units) { part = 0; th = u; }
+        else if (u < q_units + kv_units) { part = 1; th = u - q_units; }
+        else { part = 2; th = u - q_units - kv_units; }
+        const int H = part == 0 ? p.Hq : p.Hkv;
+        const int64_t t = th / H;
+        const float* src = (part == 0 ? p.q_in : part == 1 ? p.k : p.v) + th * D;
+        float x[D];
+#pragma unroll
+        for (int j = 0; j < D; j += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(src + j);
+            x[j] = a.x;
+            x[j + 1] = a.y;
+            x[j + 2] = a.z;
+            x[j + 3] = a.w;
+        }
+        if (part != 2) {
+            float sum = 0.0f;
+#pragma unroll
+            for (int j = 0; j < D; j++) sum = __fadd_rn(sum, __fmul_rn(x[j], x[j]));
+            const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)D), eps));
+            const float* w = part == 0 ? qw : kw;
+#pragma unroll
+            for (int j = 0; j < D; j++) x[j] = __fmul_rn(__fdiv_rn(x[j], rms), __ldg(w + j));
+            const int32_t pos = part == 0 ? qpos[t] : p.pos[t];
+            if ((uint64_t)pos >= (uint64_t)p.rope_cap) {
+                flag_error(p.err, kErrBounds);
+                continue;
+            }
+            const float2* cs = p.rope + (int64_t)pos * half;
+#pragma unroll
+            for (int j = 0; j < half; j++) {
+                const float2 c = __ldg(cs + j);
+                const float x1 = x[j], x2 = x[j + half];
+                x[j] = __fsub_rn(__fmul_rn(x1, c.x), __fmul_rn(x2, c.y));
+                x[j + half] = __fadd_rn(__fmul_rn(x2, c.x), __fmul_rn(x1, c.y));
+            }
+        }
+        if (part == 0) {
+            float* dst = p.q_out + th * D;
+#pragma unroll
+            for (int j = 0; j < D; j += 8) store8<float>(dst + j, x + j);
+            continue;
+        }
+        const int32_t slot = p.slots[t];
+        if ((uint64_t)slot >= (uint64_t)p.num_slots) {
+            flag_error(p.err, kErrBounds);
+            continue;
+        }
+        T* dst = reinterpret_cast<T*>(part == 1 ? p.kpool : p.vpool) + ((int64_t)slot * p.Hkv + (th % H)) * D;
+#pragma unroll
+        for (int j = 0; j < D; j += 8) store8<T>(dst + j, x + j);
+    }
+}
+
+int launch_norm_rope_append(const AppendParams& p, int dtype, const float* qw, const float* kw, float eps,
+                            const int32_t* qpos, int64_t n_q_rows, cudaStream_t stream) {
+    const int64_t units = (p.q_in ? n_q_rows * p.Hq : 0) + 2 * p.n * p.Hkv;
+    if (units <= 0) return S1KV_OK;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((units + 127) / 128, kSMs * 16));
+#define S1KV_NRA(T, DD) norm_rope_append_kernel<T, DD><<<grid, 128, 0, stream>>>(p, qw, kw, eps, qpos, n_q_rows)
+    if (p.D == 128) {
+        if (dtype == S1KV_DTYPE_F32) S1KV_NRA(float, 128);
+        else S1KV_NRA(uint16_t, 128);
+    } else if (p.D == 64) {
+        if (dtype == S1KV_DTYPE_F32) S1KV_NRA(float, 64);
+        else S1KV_NRA(uint16_t, 64);
+    } else {
+        return set_error(S1KV_EINVAL, "norm_rope_append: head_dim %d (64 or 128 supported)", p.D);
+    }
+#undef S1KV_NRA
+    g_launches++;
+    S1KV_CUDA(cudaGetLastError());
+    return S1KV_OK;
+}
+
 // ------------------------------------------------------- standalone RoPE --
 __global__ void rope_kernel(const float* __restrict__ x, float* __restrict__ out, const float2* __restrict__ tab,
                             int64_t cap, int64_t start_pos, const int32_t* __restrict__ pos_of, int64_t n, int H, int D,

@@ -94,6 +94,7 @@ SIGNATURES = {
     "s1kv_batch_begin": (C.c_int, [vp, P(u64), P(i32), P(i32), i32, vp, P(vp)]),
     "s1kv_batch_sizes": (C.c_int, [vp, P(i64), P(i64)]),
     "s1kv_batch_rope_append": (C.c_int, [vp, i32, vp, vp, i32, vp, vp, vp]),
+    "s1kv_batch_norm_rope_append": (C.c_int, [vp, i32, vp, vp, i32, vp, vp, vp, vp, f32, vp]),
     "s1kv_batch_append": (C.c_int, [vp, i32, vp, vp, vp]),
     "s1kv_batch_attention": (C.c_int, [vp, i32, vp, vp, i32, vp]),
     "s1kv_batch_layer_host": (C.c_int, [vp, i32, vp, vp, vp, vp, i32, vp]),
@@ -362,6 +363,18 @@ class Batch:
             q_out = torch.empty_like(q)
         check(self.L.s1kv_batch_rope_append(self.h, layer, _dptr(q), _dptr(q_out), q.shape[1] if q is not None else 0,
                                             _dptr(k), _dptr(v), _stream()))
+        return q_out
+
+    def norm_rope_append(self, layer, k, v, k_norm_weight, q=None, q_norm_weight=None, eps=1e-6, q_out=None):
+        """q/k RMSNorm + RoPE + append in one kernel: k, v [n_tokens, Hkv, D]
+        and q [n_rows, Hq, D] are the raw projection outputs; the norm
+        weights are fp32 CUDA [D].  Returns the normalised, rotated q."""
+        import torch
+        if q is not None and q_out is None:
+            q_out = torch.empty_like(q)
+        check(self.L.s1kv_batch_norm_rope_append(self.h, layer, _dptr(q), _dptr(q_out),
+                                                 q.shape[1] if q is not None else 0, _dptr(q_norm_weight), _dptr(k),
+                                                 _dptr(v), _dptr(k_norm_weight), eps, _stream()))
         return q_out
 
     def append(self, layer, k, v):

@@ -306,3 +306,23 @@ def test_prefix_cache_lru(oracle):
     # free list (2, 1, 0) then the LRU block 3 is evicted for the 4th block
     assert list(p.block_table(2)) == [2, 1, 0, 3]
     assert not p.is_cached(3) and p.is_cached(5)
+
+
+# ---- rmsnorm (src/nn/rmsnorm.cpp:4-33), known answers of tests/test_rmsnorm.cpp ----
+
+def test_rmsnorm_known_answers(oracle):
+    # tests/test_rmsnorm.cpp:5-14: [3, 4] with unit weight -> [0.8485, 1.1314]
+    out = oracle.rmsnorm(np.array([[3.0, 4.0]], np.float32), np.ones(2, np.float32))
+    np.testing.assert_allclose(out[0], [0.8485, 1.1314], rtol=1e-3)
+    # tests/test_rmsnorm.cpp:16-25: weight [2, 0.5] -> [1.697, 0.5657]
+    out = oracle.rmsnorm(np.array([[3.0, 4.0]], np.float32), np.array([2.0, 0.5], np.float32))
+    np.testing.assert_allclose(out[0], [1.697, 0.5657], rtol=1e-3)
+
+
+@needs_ref
+@pytest.mark.parametrize("D", [2, 64, 128])
+def test_restatement_matches_reference_rmsnorm(oracle, D):
+    rng = np.random.default_rng(40 + D)
+    x = rng.standard_normal((37, 5, D), dtype=np.float32) * 3
+    w = rng.standard_normal(D, dtype=np.float32)
+    assert np.array_equal(bits(oracle.rmsnorm(x, w)), bits(oracle.ref_rmsnorm(x, w)))
