@@ -405,7 +405,31 @@ def run_cfg3(s1kv, torch, rank, reps=10, n=256):
             b.attention(0, q_rot, out=out)
         t1.record()
         torch.cuda.synchronize()
+        # the same step's appends from raw projections: q/k RMSNorm + RoPE +
+        # append in one kernel, against the RoPE + append kernel alone
+        qw = torch.randn(D, device="cuda", generator=gen)
+        kw = torch.randn(D, device="cuda", generator=gen)
+        q_n = torch.empty_like(q)
+        ap = []
+        for fused in (True, False):
+            for _ in range(2):
+                if fused:
+                    b.norm_rope_append(0, k, v, kw, q=q, q_norm_weight=qw, q_out=q_n)
+                else:
+                    b.rope_append(0, k, v, q=q, q_out=q_n)
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record()
+            for _ in range(reps):
+                if fused:
+                    b.norm_rope_append(0, k, v, kw, q=q, q_norm_weight=qw, q_out=q_n)
+                else:
+                    b.rope_append(0, k, v, q=q, q_out=q_n)
+            a1.record()
+            torch.cuda.synchronize()
+            ap.append(a0.elapsed_time(a1) / reps)
     attn_ms = t0.elapsed_time(t1) / reps
+    # fp32 q, k, v read; q_out fp32 and K, V (bf16) written
+    ap_bytes = T * (HQ * D * 4 * 2 + 2 * HKV * D * 4 + 2 * HKV * D * 2)
     flops = prefill_flops(P, suff, HQ, D)
     cow = pool.stats()["cow_copies"]
     # 32 decode steps of all 256 sequences (split-K decode over shared blocks)
@@ -425,6 +449,8 @@ def run_cfg3(s1kv, torch, rank, reps=10, n=256):
     pool.close()
     return {"prefill_attn_ms": attn_ms, "prefill_tflops": flops / (attn_ms * 1e-3) / 1e12, "prefill_flops": flops,
             "prefill_step_ms": step_ms, "cow_copies": cow, "decode_ms_per_step": dec_ms,
+            "norm_rope_append_ms": ap[0], "norm_rope_append_gbs": ap_bytes / (ap[0] * 1e-3) / 1e9,
+            "rope_append_ms": ap[1], "append_tokens": T,
             "decode_tok_s_per_layer": n / (dec_ms * 1e-3)}
 
 
@@ -710,7 +736,10 @@ def run_ours(args):
                              "peak_source": tflops_src},
                 "prefill_attn_ms_per_layer": cfg3["prefill_attn_ms"], "prefill_flops_per_layer": cfg3["prefill_flops"],
                 "prefill_step_ms_per_layer": cfg3["prefill_step_ms"], "cow_copies": cfg3["cow_copies"],
-                "decode_ms_per_step_per_layer": cfg3["decode_ms_per_step"]},
+                "decode_ms_per_step_per_layer": cfg3["decode_ms_per_step"],
+                "norm_rope_append": {"tokens": cfg3["append_tokens"], "fused_ms": cfg3["norm_rope_append_ms"],
+                                     "fused_gbs": cfg3["norm_rope_append_gbs"],
+                                     "rope_append_only_ms": cfg3["rope_append_ms"]}},
             "cfg4_head_sharded": None if cfg4 is None else {
                 **cfg4, "roofline": {"bound": "hbm", "achieved": cfg4["kv_gbs_per_gpu"], "peak": peak,
                                      "frac": cfg4["kv_gbs_per_gpu"] / peak, "unit": "GB/s"}},

@@ -277,64 +277,81 @@ template <typename T, int D>
 __global__ void __launch_bounds__(128) norm_rope_append_kernel(const AppendParams p, const float* __restrict__ qw,
                                                                const float* __restrict__ kw, float eps,
                                                                const int32_t* __restrict__ qpos, int64_t n_q_rows) {
-    constexpr int half = D / 2;
-    const int64_t q_units = p.q_in ? n_q_rows * p.Hq : 0;
-    const int64_t kv_units = p.n * p.Hkv;
-    const int64_t total = q_units + 2 * kv_units;
-    for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
+    // Each warp moves 32 consecutive rows of one part (q, k or v) through a
+    // padded shared tile: coalesced loads, then lane i normalises and
+    // rotates row i (sequential sum, as the reference), then coalesced
+    // stores.  Rows of the tile are D + 4 floats apart (conflict-free).
+    constexpr int half = D / 2, RS = D + 4, C4 = D / 4;
+    extern __shared__ __align__(16) float tile_all[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* tile = tile_all + warp * 32 * RS;
+    const int64_t nq = p.q_in ? n_q_rows * p.Hq : 0, nk = p.n * p.Hkv;
+    const int64_t gq = (nq + 31) / 32, gk = (nk + 31) / 32;
+    const int64_t groups = gq + 2 * gk;
+    const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp, nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t gi = wid; gi < groups; gi += nwarps) {
         int part;  // 0 = q, 1 = k, 2 = v
-        int64_t th;
-        if (u < q_units) { part = 0; th = u; }
-        else if (u < q_units + kv_units) { part = 1; th = u - q_units; }
-        else { part = 2; th = u - q_units - kv_units; }
+        int64_t r0, nrows;
+        if (gi < gq) { part = 0; r0 = gi * 32; nrows = nq; }
+        else if (gi < gq + gk) { part = 1; r0 = (gi - gq) * 32; nrows = nk; }
+        else { part = 2; r0 = (gi - gq - gk) * 32; nrows = nk; }
+        const int nr = (int)(nrows - r0 < 32 ? nrows - r0 : 32);
         const int H = part == 0 ? p.Hq : p.Hkv;
-        const int64_t t = th / H;
-        const float* src = (part == 0 ? p.q_in : part == 1 ? p.k : p.v) + th * D;
-        float x[D];
-#pragma unroll
-        for (int j = 0; j < D; j += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(src + j);
-            x[j] = a.x;
-            x[j + 1] = a.y;
-            x[j + 2] = a.z;
-            x[j + 3] = a.w;
+        const float* src = (part == 0 ? p.q_in : part == 1 ? p.k : p.v) + r0 * D;
+        for (int idx = lane; idx < nr * C4; idx += 32) {
+            const int r = idx / C4, c = idx % C4;
+            *reinterpret_cast<float4*>(tile + r * RS + c * 4) = *reinterpret_cast<const float4*>(src + (int64_t)idx * 4);
         }
-        if (part != 2) {
+        __syncwarp();
+        if (part != 2 && lane < nr) {
+            float* row = tile + lane * RS;
+            const int64_t th = r0 + lane, t = th / H;
             float sum = 0.0f;
-#pragma unroll
-            for (int j = 0; j < D; j++) sum = __fadd_rn(sum, __fmul_rn(x[j], x[j]));
+#pragma unroll 8
+            for (int j = 0; j < D; j++) sum = __fadd_rn(sum, __fmul_rn(row[j], row[j]));
             const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)D), eps));
             const float* w = part == 0 ? qw : kw;
-#pragma unroll
-            for (int j = 0; j < D; j++) x[j] = __fmul_rn(__fdiv_rn(x[j], rms), __ldg(w + j));
             const int32_t pos = part == 0 ? qpos[t] : p.pos[t];
             if ((uint64_t)pos >= (uint64_t)p.rope_cap) {
                 flag_error(p.err, kErrBounds);
-                continue;
-            }
-            const float2* cs = p.rope + (int64_t)pos * half;
-#pragma unroll
-            for (int j = 0; j < half; j++) {
-                const float2 c = __ldg(cs + j);
-                const float x1 = x[j], x2 = x[j + half];
-                x[j] = __fsub_rn(__fmul_rn(x1, c.x), __fmul_rn(x2, c.y));
-                x[j + half] = __fadd_rn(__fmul_rn(x2, c.x), __fmul_rn(x1, c.y));
+            } else {
+                const float2* cs = p.rope + (int64_t)pos * half;
+#pragma unroll 4
+                for (int j = 0; j < half; j++) {
+                    const float2 c = __ldg(cs + j);
+                    const float x1 = __fmul_rn(__fdiv_rn(row[j], rms), __ldg(w + j));
+                    const float x2 = __fmul_rn(__fdiv_rn(row[j + half], rms), __ldg(w + j + half));
+                    row[j] = __fsub_rn(__fmul_rn(x1, c.x), __fmul_rn(x2, c.y));
+                    row[j + half] = __fadd_rn(__fmul_rn(x2, c.x), __fmul_rn(x1, c.y));
+                }
             }
         }
+        __syncwarp();
         if (part == 0) {
-            float* dst = p.q_out + th * D;
-#pragma unroll
-            for (int j = 0; j < D; j += 8) store8<float>(dst + j, x + j);
-            continue;
+            float* dst = p.q_out + r0 * D;
+            for (int idx = lane; idx < nr * C4; idx += 32) {
+                const int r = idx / C4, c = idx % C4;
+                *reinterpret_cast<float4*>(dst + (int64_t)idx * 4) = *reinterpret_cast<const float4*>(tile + r * RS + c * 4);
+            }
+        } else {
+            for (int idx = lane; idx < nr * C4; idx += 32) {
+                const int r = idx / C4, c = idx % C4;
+                const int64_t th = r0 + r, t = th / H;
+                const int32_t slot = p.slots[t];
+                if ((uint64_t)slot >= (uint64_t)p.num_slots) {
+                    flag_error(p.err, kErrBounds);
+                    continue;
+                }
+                T* dst = reinterpret_cast<T*>(part == 1 ? p.kpool : p.vpool) + ((int64_t)slot * p.Hkv + (th % H)) * D + c * 4;
+                const float4 x = *reinterpret_cast<const float4*>(tile + r * RS + c * 4);
+                if constexpr (sizeof(T) == 4) {
+                    *reinterpret_cast<float4*>(dst) = x;
+                } else {
+                    *reinterpret_cast<uint2*>(dst) = make_uint2((uint32_t)f32_to_bf16(x.x) | ((uint32_t)f32_to_bf16(x.y) << 16), (uint32_t)f32_to_bf16(x.z) | ((uint32_t)f32_to_bf16(x.w) << 16));
+                }
+            }
         }
-        const int32_t slot = p.slots[t];
-        if ((uint64_t)slot >= (uint64_t)p.num_slots) {
-            flag_error(p.err, kErrBounds);
-            continue;
-        }
-        T* dst = reinterpret_cast<T*>(part == 1 ? p.kpool : p.vpool) + ((int64_t)slot * p.Hkv + (th % H)) * D;
-#pragma unroll
-        for (int j = 0; j < D; j += 8) store8<T>(dst + j, x + j);
+        __syncwarp();
     }
 }
 
@@ -343,7 +360,13 @@ int launch_norm_rope_append(const AppendParams& p, int dtype, const float* qw, c
     const int64_t units = (p.q_in ? n_q_rows * p.Hq : 0) + 2 * p.n * p.Hkv;
     if (units <= 0) return S1KV_OK;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((units + 127) / 128, kSMs * 16));
-#define S1KV_NRA(T, DD) norm_rope_append_kernel<T, DD><<<grid, 128, 0, stream>>>(p, qw, kw, eps, qpos, n_q_rows)
+    // 4 warps, each a 32-row tile of head_dim + 4 floats per row
+#define S1KV_NRA(T, DD)                                                                                     \
+    do {                                                                                                   \
+        const int sm = 4 * 32 * (DD + 4) * 4;                                                              \
+        S1KV_CUDA(cudaFuncSetAttribute(norm_rope_append_kernel<T, DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm)); \
+        norm_rope_append_kernel<T, DD><<<grid, 128, sm, stream>>>(p, qw, kw, eps, qpos, n_q_rows);        \
+    } while (0)
     if (p.D == 128) {
         if (dtype == S1KV_DTYPE_F32) S1KV_NRA(float, 128);
         else S1KV_NRA(uint16_t, 128);
