@@ -298,6 +298,13 @@ int s1kv_batch_rope_append(s1kv_batch* batch, int32_t layer, const float* q_in, 
 int s1kv_batch_norm_rope_append(s1kv_batch* batch, int32_t layer, const float* q_in, float* q_out, int32_t n_q_heads,
                                 const float* q_norm_weight, const float* k, const float* v, const float* k_norm_weight,
                                 float eps, void* stream);
+
+/* Self-check of the division the fused norm kernel uses (no reference
+ * counterpart; test support): adds to *mismatch (device, unsigned long long)
+ * the number of (x, d) pairs, x from xs[nx] and d from ds[nd] (device
+ * arrays), on which it differs from the correctly rounded x / d. */
+int s1kv_debug_div_check(const float* xs, int64_t nx, const float* ds, int64_t nd, unsigned long long* mismatch,
+                         void* stream);
 /* Append without RoPE (KVBlockPool::append data movement). */
 int s1kv_batch_append(s1kv_batch* batch, int32_t layer, const float* k, const float* v, void* stream);
 /* Paged GQA attention of the batch's query rows (post-RoPE q). */

@@ -266,6 +266,20 @@ int launch_append(const AppendParams& p, int dtype, bool rope, cudaStream_t stre
 }
 
 // ------------------------------------------- q/k RMSNorm + RoPE + append --
+// x / d correctly rounded from r = RN(1 / d), for many x over one d:
+// Markstein's FMA correction (P. Markstein, IBM J. Res. Dev. 34(1), 1990;
+// Muller et al., Handbook of Floating-Point Arithmetic, division by FMA):
+// q0 = RN(x r), the residual e = x - q0 d is exact in one FMA, and
+// RN(q0 + e r) is the correctly rounded quotient.  e == 0 keeps q0 (exact
+// quotients, and the sign of a zero x).  Checked against __fdiv_rn by
+// s1kv_debug_div_check on millions of inputs.
+__device__ __forceinline__ float div_by(float x, float d, float r) {
+    const float q0 = __fmul_rn(x, r);
+    const float e = __fmaf_rn(-q0, d, x);
+    return e == 0.0f ? q0 : __fmaf_rn(e, r, q0);
+}
+
+
 // The projection outputs of one step straight into the cache
 // (src/nn/attention.cpp:316-322): q and k rows are RMS-normalised with their
 // weights (src/nn/rmsnorm.cpp:4-33: squares summed in order, sqrt(sum / D +
@@ -278,9 +292,11 @@ __global__ void __launch_bounds__(128) norm_rope_append_kernel(const AppendParam
                                                                const float* __restrict__ kw, float eps,
                                                                const int32_t* __restrict__ qpos, int64_t n_q_rows) {
     // Each warp moves 32 consecutive rows of one part (q, k or v) through a
-    // padded shared tile: coalesced loads, then lane i normalises and
-    // rotates row i (sequential sum, as the reference), then coalesced
-    // stores.  Rows of the tile are D + 4 floats apart (conflict-free).
+    // shared tile: asynchronous 16-byte copies (all of the tile's 16 KB in
+    // flight at once), then lane i normalises and rotates row i in registers
+    // (sequential sum, as the reference), then coalesced stores.  Tile rows
+    // are D + 4 floats apart: 16-byte aligned, and the lanes' float4 row
+    // accesses take the minimum number of shared-memory wavefronts.
     constexpr int half = D / 2, RS = D + 4, C4 = D / 4;
     extern __shared__ __align__(16) float tile_all[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -298,56 +314,72 @@ __global__ void __launch_bounds__(128) norm_rope_append_kernel(const AppendParam
         const int nr = (int)(nrows - r0 < 32 ? nrows - r0 : 32);
         const int H = part == 0 ? p.Hq : p.Hkv;
         const float* src = (part == 0 ? p.q_in : part == 1 ? p.k : p.v) + r0 * D;
-        for (int idx = lane; idx < nr * C4; idx += 32) {
-            const int r = idx / C4, c = idx % C4;
-            *reinterpret_cast<float4*>(tile + r * RS + c * 4) = *reinterpret_cast<const float4*>(src + (int64_t)idx * 4);
-        }
+        for (int idx = lane; idx < nr * C4; idx += 32)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                             (uint32_t)__cvta_generic_to_shared(tile + (idx / C4) * RS + (idx % C4) * 4)),
+                         "l"(src + (int64_t)idx * 4)
+                         : "memory");
+        asm volatile("cp.async.wait_all;" ::: "memory");
         __syncwarp();
         if (part != 2 && lane < nr) {
             float* row = tile + lane * RS;
             const int64_t th = r0 + lane, t = th / H;
+            float x[D];
+#pragma unroll
+            for (int j = 0; j < D; j += 4) {
+                const float4 a = *reinterpret_cast<const float4*>(row + j);
+                x[j] = a.x;
+                x[j + 1] = a.y;
+                x[j + 2] = a.z;
+                x[j + 3] = a.w;
+            }
             float sum = 0.0f;
-#pragma unroll 8
-            for (int j = 0; j < D; j++) sum = __fadd_rn(sum, __fmul_rn(row[j], row[j]));
+#pragma unroll
+            for (int j = 0; j < D; j++) sum = __fadd_rn(sum, __fmul_rn(x[j], x[j]));
             const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)D), eps));
+            const float rrms = __frcp_rn(rms);
             const float* w = part == 0 ? qw : kw;
             const int32_t pos = part == 0 ? qpos[t] : p.pos[t];
             if ((uint64_t)pos >= (uint64_t)p.rope_cap) {
                 flag_error(p.err, kErrBounds);
             } else {
                 const float2* cs = p.rope + (int64_t)pos * half;
-#pragma unroll 4
+#pragma unroll
                 for (int j = 0; j < half; j++) {
                     const float2 c = __ldg(cs + j);
-                    const float x1 = __fmul_rn(__fdiv_rn(row[j], rms), __ldg(w + j));
-                    const float x2 = __fmul_rn(__fdiv_rn(row[j + half], rms), __ldg(w + j + half));
-                    row[j] = __fsub_rn(__fmul_rn(x1, c.x), __fmul_rn(x2, c.y));
-                    row[j + half] = __fadd_rn(__fmul_rn(x2, c.x), __fmul_rn(x1, c.y));
+                    const float x1 = __fmul_rn(div_by(x[j], rms, rrms), __ldg(w + j));
+                    const float x2 = __fmul_rn(div_by(x[j + half], rms, rrms), __ldg(w + j + half));
+                    x[j] = __fsub_rn(__fmul_rn(x1, c.x), __fmul_rn(x2, c.y));
+                    x[j + half] = __fadd_rn(__fmul_rn(x2, c.x), __fmul_rn(x1, c.y));
                 }
+#pragma unroll
+                for (int j = 0; j < D; j += 4)
+                    *reinterpret_cast<float4*>(row + j) = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
             }
         }
         __syncwarp();
         if (part == 0) {
             float* dst = p.q_out + r0 * D;
-            for (int idx = lane; idx < nr * C4; idx += 32) {
-                const int r = idx / C4, c = idx % C4;
-                *reinterpret_cast<float4*>(dst + (int64_t)idx * 4) = *reinterpret_cast<const float4*>(tile + r * RS + c * 4);
-            }
+            for (int idx = lane; idx < nr * C4; idx += 32)
+                *reinterpret_cast<float4*>(dst + (int64_t)idx * 4) =
+                    *reinterpret_cast<const float4*>(tile + (idx / C4) * RS + (idx % C4) * 4);
         } else {
+            // four elements per lane: 8-byte (bf16) or 16-byte stores
             for (int idx = lane; idx < nr * C4; idx += 32) {
-                const int r = idx / C4, c = idx % C4;
+                const int r = idx / C4, c = (idx % C4) * 4;
                 const int64_t th = r0 + r, t = th / H;
                 const int32_t slot = p.slots[t];
                 if ((uint64_t)slot >= (uint64_t)p.num_slots) {
                     flag_error(p.err, kErrBounds);
                     continue;
                 }
-                T* dst = reinterpret_cast<T*>(part == 1 ? p.kpool : p.vpool) + ((int64_t)slot * p.Hkv + (th % H)) * D + c * 4;
-                const float4 x = *reinterpret_cast<const float4*>(tile + r * RS + c * 4);
+                T* dst = reinterpret_cast<T*>(part == 1 ? p.kpool : p.vpool) + ((int64_t)slot * p.Hkv + (th % H)) * D + c;
+                const float4 a = *reinterpret_cast<const float4*>(tile + r * RS + c);
                 if constexpr (sizeof(T) == 4) {
-                    *reinterpret_cast<float4*>(dst) = x;
+                    *reinterpret_cast<float4*>(dst) = a;
                 } else {
-                    *reinterpret_cast<uint2*>(dst) = make_uint2((uint32_t)f32_to_bf16(x.x) | ((uint32_t)f32_to_bf16(x.y) << 16), (uint32_t)f32_to_bf16(x.z) | ((uint32_t)f32_to_bf16(x.w) << 16));
+                    *reinterpret_cast<uint2*>(dst) = make_uint2((uint32_t)f32_to_bf16(a.x) | ((uint32_t)f32_to_bf16(a.y) << 16),
+                                                                (uint32_t)f32_to_bf16(a.z) | ((uint32_t)f32_to_bf16(a.w) << 16));
                 }
             }
         }
@@ -455,3 +487,24 @@ int launch_gather(s1kv_pool* p, int32_t layer, int32_t row, int64_t len, int whi
 }
 
 }  // namespace s1kv
+
+// ----------------------------------------------------------- self-check --
+namespace s1kv {
+// Counts the (x, d) pairs on which div_by differs from __fdiv_rn: x from
+// xs, d from ds (all pairs), result added to *mismatch (device).
+__global__ void div_check_kernel(const float* xs, int64_t nx, const float* ds, int64_t nd, unsigned long long* mismatch) {
+    const int64_t total = nx * nd;
+    unsigned long long bad = 0;
+    for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total; u += (int64_t)gridDim.x * blockDim.x) {
+        const float x = xs[u % nx], d = ds[u / nx];
+        if (__float_as_uint(div_by(x, d, __frcp_rn(d))) != __float_as_uint(__fdiv_rn(x, d))) bad++;
+    }
+    if (bad) atomicAdd(mismatch, bad);
+}
+}  // namespace s1kv
+
+extern "C" int s1kv_debug_div_check(const float* xs, int64_t nx, const float* ds, int64_t nd,
+                                   unsigned long long* mismatch, void* stream) {
+    s1kv::div_check_kernel<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(xs, nx, ds, nd, mismatch);
+    return cudaGetLastError() == cudaSuccess ? S1KV_OK : S1KV_ECUDA;
+}

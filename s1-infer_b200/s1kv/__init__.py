@@ -95,6 +95,7 @@ SIGNATURES = {
     "s1kv_batch_sizes": (C.c_int, [vp, P(i64), P(i64)]),
     "s1kv_batch_rope_append": (C.c_int, [vp, i32, vp, vp, i32, vp, vp, vp]),
     "s1kv_batch_norm_rope_append": (C.c_int, [vp, i32, vp, vp, i32, vp, vp, vp, vp, f32, vp]),
+    "s1kv_debug_div_check": (C.c_int, [vp, i64, vp, i64, vp, vp]),
     "s1kv_batch_append": (C.c_int, [vp, i32, vp, vp, vp]),
     "s1kv_batch_attention": (C.c_int, [vp, i32, vp, vp, i32, vp]),
     "s1kv_batch_layer_host": (C.c_int, [vp, i32, vp, vp, vp, vp, i32, vp]),

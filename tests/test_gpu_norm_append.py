@@ -63,3 +63,23 @@ def test_norm_rope_append_matches_reference_chain(s1kv, oracle, cuda, dtype, D):
         assert np.array_equal(kst[slot], enc(_chain(oracle, k2[i:i + 1], kw, [T[s - 1]]))[0])
     assert pool.check_device() == 0
     pool.close()
+
+
+@pytest.mark.gpu
+def test_fused_norm_division_is_correctly_rounded(s1kv, cuda):
+    """The normalisation divides each element by the row's rms with a
+    reciprocal and one FMA correction; on 2^12 numerators x 2^11 divisors
+    (random magnitudes over 2^-20 .. 2^20, both signs, zeros, rms-like values
+    around 1e-3 .. 1e3) it equals the correctly rounded quotient bit for bit."""
+    import torch
+    rng = np.random.default_rng(99)
+    xs = (rng.standard_normal(4096) * np.exp2(rng.uniform(-20, 20, 4096))).astype(np.float32)
+    xs[:4] = [0.0, -0.0, 1.0, -3.0]
+    ds = np.concatenate([np.exp2(rng.uniform(-10, 10, 1024)),
+                         np.sqrt(rng.uniform(1e-6, 1e6, 1024))]).astype(np.float32)
+    bad = torch.zeros(1, dtype=torch.int64, device="cuda")
+    L = s1kv.lib()
+    assert L.s1kv_debug_div_check(torch.from_numpy(xs).cuda().data_ptr(), xs.size, torch.from_numpy(ds).cuda().data_ptr(),
+                                  ds.size, bad.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    assert int(bad.item()) == 0
