@@ -324,18 +324,16 @@ __global__ void __launch_bounds__(128) norm_rope_append_kernel(const AppendParam
         if (part != 2 && lane < nr) {
             float* row = tile + lane * RS;
             const int64_t th = r0 + lane, t = th / H;
-            float x[D];
-#pragma unroll
+            // pass 1: the sum of squares in order, straight from the tile
+            float sum = 0.0f;
+#pragma unroll 8
             for (int j = 0; j < D; j += 4) {
                 const float4 a = *reinterpret_cast<const float4*>(row + j);
-                x[j] = a.x;
-                x[j + 1] = a.y;
-                x[j + 2] = a.z;
-                x[j + 3] = a.w;
+                sum = __fadd_rn(sum, __fmul_rn(a.x, a.x));
+                sum = __fadd_rn(sum, __fmul_rn(a.y, a.y));
+                sum = __fadd_rn(sum, __fmul_rn(a.z, a.z));
+                sum = __fadd_rn(sum, __fmul_rn(a.w, a.w));
             }
-            float sum = 0.0f;
-#pragma unroll
-            for (int j = 0; j < D; j++) sum = __fadd_rn(sum, __fmul_rn(x[j], x[j]));
             const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)D), eps));
             const float rrms = __frcp_rn(rms);
             const float* w = part == 0 ? qw : kw;
@@ -343,18 +341,25 @@ __global__ void __launch_bounds__(128) norm_rope_append_kernel(const AppendParam
             if ((uint64_t)pos >= (uint64_t)p.rope_cap) {
                 flag_error(p.err, kErrBounds);
             } else {
+                // pass 2: normalise, weight and rotate four pairs at a time, in place
                 const float2* cs = p.rope + (int64_t)pos * half;
+#pragma unroll 2
+                for (int j = 0; j < half; j += 4) {
+                    const float4 l4 = *reinterpret_cast<const float4*>(row + j);
+                    const float4 h4 = *reinterpret_cast<const float4*>(row + j + half);
+                    const float lo[4] = {l4.x, l4.y, l4.z, l4.w}, hi[4] = {h4.x, h4.y, h4.z, h4.w};
+                    float ro[4], rh[4];
 #pragma unroll
-                for (int j = 0; j < half; j++) {
-                    const float2 c = __ldg(cs + j);
-                    const float x1 = __fmul_rn(div_by(x[j], rms, rrms), __ldg(w + j));
-                    const float x2 = __fmul_rn(div_by(x[j + half], rms, rrms), __ldg(w + j + half));
-                    x[j] = __fsub_rn(__fmul_rn(x1, c.x), __fmul_rn(x2, c.y));
-                    x[j + half] = __fadd_rn(__fmul_rn(x2, c.x), __fmul_rn(x1, c.y));
+                    for (int e = 0; e < 4; e++) {
+                        const float2 c = __ldg(cs + j + e);
+                        const float x1 = __fmul_rn(div_by(lo[e], rms, rrms), __ldg(w + j + e));
+                        const float x2 = __fmul_rn(div_by(hi[e], rms, rrms), __ldg(w + j + e + half));
+                        ro[e] = __fsub_rn(__fmul_rn(x1, c.x), __fmul_rn(x2, c.y));
+                        rh[e] = __fadd_rn(__fmul_rn(x2, c.x), __fmul_rn(x1, c.y));
+                    }
+                    *reinterpret_cast<float4*>(row + j) = make_float4(ro[0], ro[1], ro[2], ro[3]);
+                    *reinterpret_cast<float4*>(row + j + half) = make_float4(rh[0], rh[1], rh[2], rh[3]);
                 }
-#pragma unroll
-                for (int j = 0; j < D; j += 4)
-                    *reinterpret_cast<float4*>(row + j) = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
             }
         }
         __syncwarp();
@@ -364,11 +369,15 @@ __global__ void __launch_bounds__(128) norm_rope_append_kernel(const AppendParam
                 *reinterpret_cast<float4*>(dst + (int64_t)idx * 4) =
                     *reinterpret_cast<const float4*>(tile + (idx / C4) * RS + (idx % C4) * 4);
         } else {
-            // four elements per lane: 8-byte (bf16) or 16-byte stores
-            for (int idx = lane; idx < nr * C4; idx += 32) {
-                const int r = idx / C4, c = (idx % C4) * 4;
-                const int64_t th = r0 + r, t = th / H;
-                const int32_t slot = p.slots[t];
+            // four elements per lane: 8-byte (bf16) or 16-byte stores; lane i
+            // looks up row i's slot once and the warp shares it by shuffle
+            const int32_t my_slot = lane < nr ? p.slots[(r0 + lane) / H] : 0;
+            for (int base = 0; base < nr * C4; base += 32) {  // warp-uniform trip count (shuffle inside)
+                const int idx = base + lane;
+                const int r = min(idx / C4, nr - 1), c = (idx % C4) * 4;
+                const int32_t slot = __shfl_sync(0xffffffffu, my_slot, r);
+                if (idx >= nr * C4) continue;
+                const int64_t th = r0 + r;
                 if ((uint64_t)slot >= (uint64_t)p.num_slots) {
                     flag_error(p.err, kErrBounds);
                     continue;
