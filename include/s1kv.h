@@ -185,6 +185,28 @@ int s1kv_prefix_save(s1kv_pool* pool, uint64_t seq, const char* path);
  * is missing or short (the reference returns false). */
 int s1kv_prefix_load(s1kv_pool* pool, uint64_t seq, int64_t n_tokens, const char* path);
 
+/* Versioned prefix file (format 1; no reference counterpart): supersedes
+ * the raw dump above with a 64-byte header (magic "S1KVPFX", version, shape,
+ * payload dtype, token count, RoPE theta, FNV-1a 64 checksum of the body),
+ * optional token ids, then K and V of every layer in the pool dtype.  The
+ * layout is documented in s1-infer_b200/csrc/prefix_file.cpp. */
+typedef struct s1kv_prefix_info {
+    int32_t version, num_layers, num_kv_heads, head_dim, block_size, dtype, has_tokens;
+    int64_t n_tokens;
+    float rope_theta;
+} s1kv_prefix_info;
+/* Writes seq's K/V of every layer; token_ids (host, length = seq length)
+ * may be NULL. */
+int s1kv_prefix_save_v1(s1kv_pool* pool, uint64_t seq, const int32_t* token_ids, const char* path);
+/* Reads and verifies a file's header and checksum (host only, no device). */
+int s1kv_prefix_file_info(const char* path, s1kv_prefix_info* info);
+/* Creates seq (must not exist) from a file: S1KV_EINVAL on a bad magic,
+ * version, size, checksum, shape or RoPE theta mismatch.  register_blocks:
+ * also enter its full blocks into the hashed prefix cache under the stored
+ * token ids, so later prompts share them.  *n_tokens_out may be NULL. */
+int s1kv_prefix_load_v1(s1kv_pool* pool, uint64_t seq, const char* path, int32_t register_blocks,
+                        int64_t* n_tokens_out);
+
 /* ======================== kernels (device, async) ======================== */
 
 /* Runs queued copy-on-write block copies and device block-table updates. */

@@ -49,6 +49,19 @@ class PoolDesc(C.Structure):
                 ("rope_theta", f32), ("flags", i32), ("initial_free_list", P(i32))]
 
 
+class PrefixInfo(C.Structure):
+    _fields_ = [("version", i32), ("num_layers", i32), ("num_kv_heads", i32), ("head_dim", i32), ("block_size", i32),
+                ("dtype", i32), ("has_tokens", i32), ("n_tokens", i64), ("rope_theta", f32)]
+
+
+def prefix_file_info(path):
+    """Header of a format-1 prefix file, after checking its size and checksum
+    (host only)."""
+    info = PrefixInfo()
+    check(lib().s1kv_prefix_file_info(str(path).encode(), C.byref(info)))
+    return {f: getattr(info, f) for f, _ in PrefixInfo._fields_}
+
+
 class PoolStats(C.Structure):
     _fields_ = [("num_free", i64), ("num_lru", i64), ("num_cached", i64), ("num_seqs", i64),
                 ("cow_copies", i64), ("evictions", i64), ("device_bytes", i64)]
@@ -94,6 +107,9 @@ SIGNATURES = {
     "s1kv_batch_begin": (C.c_int, [vp, P(u64), P(i32), P(i32), i32, vp, P(vp)]),
     "s1kv_batch_sizes": (C.c_int, [vp, P(i64), P(i64)]),
     "s1kv_batch_rope_append": (C.c_int, [vp, i32, vp, vp, i32, vp, vp, vp]),
+    "s1kv_prefix_save_v1": (C.c_int, [vp, u64, P(i32), C.c_char_p]),
+    "s1kv_prefix_file_info": (C.c_int, [C.c_char_p, vp]),
+    "s1kv_prefix_load_v1": (C.c_int, [vp, u64, C.c_char_p, i32, P(i64)]),
     "s1kv_batch_norm_rope_append": (C.c_int, [vp, i32, vp, vp, i32, vp, vp, vp, vp, f32, vp]),
     "s1kv_debug_div_check": (C.c_int, [vp, i64, vp, i64, vp, vp]),
     "s1kv_batch_append": (C.c_int, [vp, i32, vp, vp, vp]),
@@ -268,6 +284,15 @@ class Pool:
 
     def prefix_save(self, seq, path):
         check(self.L.s1kv_prefix_save(self.h, seq, str(path).encode()))
+
+    def prefix_save_v1(self, seq, path, tokens=None):
+        t = None if tokens is None else np.ascontiguousarray(tokens, dtype=np.int32)
+        check(self.L.s1kv_prefix_save_v1(self.h, seq, _i32p(t), str(path).encode()))
+
+    def prefix_load_v1(self, seq, path, register=False):
+        n = i64()
+        check(self.L.s1kv_prefix_load_v1(self.h, seq, str(path).encode(), int(register), C.byref(n)))
+        return n.value
 
     def prefix_load(self, seq, n_tokens, path):
         check(self.L.s1kv_prefix_load(self.h, seq, n_tokens, str(path).encode()))
