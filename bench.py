@@ -500,38 +500,56 @@ def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3):
     gbuf = torch.empty((world, B, hq, D), device="cuda")
     nxt = (rank + 1) % world
 
-    def step(ev=None):
+    ex = s1kv.PeerExchange(rank, world, B, hq_all, D)
+    epoch = [0]
+
+    def step(ev=None, fused=False):
         q = q0
         with pool.batch(seqs, [1] * B) as bt:
             for layer in range(layers):
                 bt.rope_append(layer, kn[layer], vn[layer], q=q, q_out=q_rot)
                 if ev is not None:
                     ev[layer][0].record()
-                bt.attention(layer, q_rot, out=out)
-                if ev is not None:
-                    ev[layer][1].record()
-                full = s1kv.gather_heads(out, world, buf=gbuf)  # [B, 64, 128] token-major on every rank
+                if fused:
+                    # the decode kernels store every finished row into all
+                    # ranks' token-major buffers over NVLink, then signal
+                    epoch[0] += 1
+                    ex.attention(bt, layer, q_rot, q_lo, epoch[0])
+                    if ev is not None:
+                        ev[layer][1].record()
+                    ex.wait(epoch[0])
+                    full = ex.output(epoch[0])
+                else:
+                    bt.attention(layer, q_rot, out=out)
+                    if ev is not None:
+                        ev[layer][1].record()
+                    full = s1kv.gather_heads(out, world, buf=gbuf)  # [B, 64, 128] token-major on every rank
                 if ev is not None:
                     ev[layer][2].record()
                 q = full[:, nxt * hq:(nxt + 1) * hq].contiguous()
 
-    for _ in range(warmup):
-        step()
-    barrier(torch, world)
-    torch.cuda.synchronize()
-    ctx_before = [pool.length(s) for s in seqs]
-    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(layers)] for _ in range(steps)]
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for i in range(steps):
-        step(evs[i])
-    t1.record()
-    torch.cuda.synchronize()
-    elapsed = max_over_ranks(torch, world, t0.elapsed_time(t1))
-    attn_ms = float(np.mean([evs[i][l][0].elapsed_time(evs[i][l][1]) for i in range(steps) for l in range(layers)]))
-    gather_ms = float(np.mean([evs[i][l][1].elapsed_time(evs[i][l][2]) for i in range(steps) for l in range(layers)]))
-    attn_ms = max_over_ranks(torch, world, attn_ms)
-    gather_ms = max_over_ranks(torch, world, gather_ms)
+    res = {}
+    for mode in ("nccl", "fused"):
+        fused = mode == "fused"
+        for _ in range(warmup):
+            step(fused=fused)
+        barrier(torch, world)
+        torch.cuda.synchronize()
+        ctx_before = [pool.length(s) for s in seqs]
+        evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(layers)] for _ in range(steps)]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(steps):
+            step(evs[i], fused=fused)
+        t1.record()
+        torch.cuda.synchronize()
+        elapsed = max_over_ranks(torch, world, t0.elapsed_time(t1))
+        attn_ms = float(np.mean([evs[i][l][0].elapsed_time(evs[i][l][1]) for i in range(steps) for l in range(layers)]))
+        xchg_ms = float(np.mean([evs[i][l][1].elapsed_time(evs[i][l][2]) for i in range(steps) for l in range(layers)]))
+        res[mode] = (elapsed, max_over_ranks(torch, world, attn_ms), max_over_ranks(torch, world, xchg_ms), ctx_before)
+    s1kv.device_check(torch.cuda.current_device())
+    ex.close()
+    elapsed, attn_ms, gather_ms, ctx_before = res["fused"]
     # algorithmic bytes of one layer's attention on this GPU: K and V of the
     # local heads once, q in and out (fp32), block ids
     ctx_mid = [c + (steps + 1) // 2 for c in ctx_before]
@@ -541,12 +559,16 @@ def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3):
     del q0, kn, vn, q_rot, out, gbuf
     torch.cuda.empty_cache()
     step_ms_80 = elapsed / steps * CFG4_LAYERS / layers
+    nccl_step_80 = res["nccl"][0] / steps * CFG4_LAYERS / layers
     return {"workload": "cfg4: 4 seqs x ctx 131072, Hq64/Hkv8/D128, bf16, 80 layers, pool 1.1x scattered (seed 3)",
-            "parallelism": f"kv-head-sharded x{world} ({hkv} KV heads per GPU), NCCL all-gather per layer",
+            "parallelism": f"kv-head-sharded x{world} ({hkv} KV heads per GPU); finished rows stored into every "
+                           f"rank's buffer over NVLink by the decode kernels (fused exchange)",
+            "nccl_allgather": {"ms_per_step_80_layers": nccl_step_80, "tok_s": B / (nccl_step_80 * 1e-3),
+                               "allgather_reorder_ms_per_layer": res["nccl"][2]},
             "scaling": "strong", "layers_timed": layers, "steps": steps,
             "ms_per_step_80_layers": step_ms_80, "tok_s": B / (step_ms_80 * 1e-3),
             "ms_per_layer": elapsed / steps / layers, "attn_ms_per_layer": attn_ms,
-            "allgather_reorder_ms_per_layer": gather_ms,
+            "exchange_wait_ms_per_layer": gather_ms,
             "attn_bytes_per_layer_per_gpu": attn_bytes, "kv_gbs_per_gpu": attn_bytes / (attn_ms * 1e-3) / 1e9}
 
 

@@ -207,6 +207,33 @@ int s1kv_prefix_file_info(const char* path, s1kv_prefix_info* info);
 int s1kv_prefix_load_v1(s1kv_pool* pool, uint64_t seq, const char* path, int32_t register_blocks,
                         int64_t* n_tokens_out);
 
+/* ============ KV-head sharding: output exchange between GPUs ============ */
+/* No reference counterpart (s1-infer is single-process).  One process per
+ * GPU; rank r keeps KV heads [r*Hkv/N, (r+1)*Hkv/N) and their query heads.
+ * Each rank creates an exchange holding two layer slots of the token-major
+ * output [rows][all query heads][head_dim] (fp32, slot_floats floats each;
+ * layers alternate by epoch parity), exports its CUDA IPC handle (64 bytes),
+ * and opens every peer's from the array of all ranks' handles (world x 64
+ * bytes, in rank order).  s1kv_batch_attention_exchange runs a decode
+ * batch's attention for this rank's heads and stores each finished row into
+ * its place in every rank's slot over NVLink, then signals `epoch`;
+ * s1kv_exchange_wait (device, bounded: sets the timeout bit of the error word
+ * after about a second) makes the stream wait until all ranks signalled it.
+ * Epochs increase by one per layer step. */
+typedef struct s1kv_exchange s1kv_exchange;
+int s1kv_exchange_create(int device, int32_t rank, int32_t world, int64_t slot_floats, s1kv_exchange** out);
+int s1kv_exchange_handle(const s1kv_exchange* ex, void* handle64);
+int s1kv_exchange_open(s1kv_exchange* ex, const void* handles);
+/* Device address of the slot `epoch` uses: [rows][heads_total][head_dim]. */
+float* s1kv_exchange_buffer(const s1kv_exchange* ex, uint32_t epoch);
+int s1kv_exchange_wait(s1kv_exchange* ex, uint32_t epoch, void* stream);
+int s1kv_exchange_destroy(s1kv_exchange* ex);
+/* Decode attention of this rank's n_q_heads query heads (first global head
+ * head0 of heads_total), output published through the exchange. */
+int s1kv_batch_attention_exchange(s1kv_batch* batch, int32_t layer, const float* q, int32_t n_q_heads,
+                                  s1kv_exchange* ex, int32_t head0, int32_t heads_total, uint32_t epoch,
+                                  void* stream);
+
 /* ======================== kernels (device, async) ======================== */
 
 /* Runs queued copy-on-write block copies and device block-table updates. */

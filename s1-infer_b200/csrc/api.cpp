@@ -346,42 +346,16 @@ int s1kv_batch_append(s1kv_batch* b, int32_t layer, const float* k, const float*
     return batch_append_impl(b, layer, nullptr, nullptr, 0, k, v, false, (cudaStream_t)stream);
 }
 
-int s1kv_batch_attention(s1kv_batch* b, int32_t layer, const float* q, float* out, int32_t Hq, void* stream_) {
-    if (!b) return set_error(S1KV_EINVAL, "null batch");
+}  // extern "C"
+
+// The split-K decode path of s1kv_batch_attention; `ex` (optional) places the
+// finished rows into the peer exchange.
+static int split_k_attention(s1kv_batch* b, int32_t layer, const float* q, float* out, int32_t Hq,
+                             const AttnParams* ex, cudaStream_t stream) {
     s1kv_pool* p = b->pool;
-    int st = check_layer(p, layer);
-    if (st) return st;
-    S1KV_ON_DEVICE(p->device);
+    int st = S1KV_OK;
     const int32_t Hkv = p->desc.num_kv_heads, D = p->desc.head_dim;
-    if (Hq <= 0 || Hq % Hkv) return set_error(S1KV_EINVAL, "s1kv_batch_attention: n_q_heads must be a multiple of num_kv_heads");
-    if (b->n_rows == 0) return S1KV_OK;
-    if (!q || !out) return set_error(S1KV_EINVAL, "s1kv_batch_attention: null q/out");
     const int G = Hq / Hkv;
-    cudaStream_t stream = (cudaStream_t)stream_;
-    // Chunks of several query rows per sequence over bf16 K/V are a dense
-    // contraction: tensor-core prefill.  Decode rows stay on the split-K
-    // kernel.
-    // (q and out are read and written by TMA there: 16-byte aligned.)
-    if (!b->decode_rows && p->tmap_sw_ok && prefill_tc_supported(p->desc.dtype, D, G, p->desc.block_size) &&
-        (((uintptr_t)q | (uintptr_t)out) & 15) == 0) {
-        PrefillParams pp{};
-        pp.q = q;
-        pp.out = out;
-        pp.table = p->d_table;
-        pp.seqs = b->d_pseqs;
-        pp.n_seqs = b->n_seqs;
-        pp.max_chunks = (b->max_qlen + prefill_queries_per_cta(G) - 1) / prefill_queries_per_cta(G);
-        pp.max_bps = p->max_bps;
-        pp.max_blocks = (int32_t)p->desc.max_blocks;
-        pp.Hq = Hq;
-        pp.Hkv = Hkv;
-        pp.layer = layer;
-        pp.scale_log2 = scale_log2(D);
-        pp.n_rows = b->n_rows;
-        pp.err = p->d_err;
-        if (pp.n_seqs == 0 || pp.max_chunks == 0) return S1KV_OK;
-        return launch_prefill_tc(pp, p->tmap_k_sw, p->tmap_v_sw, stream);
-    }
     if (!b->items_uploaded) {
         // A query-chunk batch on the split-K kernels (shapes or alignments the
         // tensor-core prefill does not take): plan and upload its work list.
@@ -432,7 +406,83 @@ int s1kv_batch_attention(s1kv_batch* b, int32_t layer, const float* q, float* ou
         S1KV_CUDA(cudaMemsetAsync(p->counters.p, 0, p->counters.cap, stream));
     }
     ap.counters = (int32_t*)p->counters.p;
+    if (ex) {
+        ap.out_stride = ex->out_stride;
+        ap.out_head0 = ex->out_head0;
+        ap.n_peers = ex->n_peers;
+        for (int k = 0; k < 7; k++) ap.peer_out[k] = ex->peer_out[k];
+        ap.done = ex->done;
+        ap.done_total = (int32_t)(b->n_rows * Hkv);
+        ap.n_flags = ex->n_flags;
+        for (int k = 0; k < 8; k++) ap.flag_dst[k] = ex->flag_dst[k];
+        ap.epoch = ex->epoch;
+    }
     return launch_attention(p, ap, p->desc.dtype, stream);
+}
+
+extern "C" {
+
+int s1kv_batch_attention(s1kv_batch* b, int32_t layer, const float* q, float* out, int32_t Hq, void* stream_) {
+    if (!b) return set_error(S1KV_EINVAL, "null batch");
+    s1kv_pool* p = b->pool;
+    int st = check_layer(p, layer);
+    if (st) return st;
+    S1KV_ON_DEVICE(p->device);
+    const int32_t Hkv = p->desc.num_kv_heads, D = p->desc.head_dim;
+    if (Hq <= 0 || Hq % Hkv) return set_error(S1KV_EINVAL, "s1kv_batch_attention: n_q_heads must be a multiple of num_kv_heads");
+    if (b->n_rows == 0) return S1KV_OK;
+    if (!q || !out) return set_error(S1KV_EINVAL, "s1kv_batch_attention: null q/out");
+    const int G = Hq / Hkv;
+    cudaStream_t stream = (cudaStream_t)stream_;
+    // Chunks of several query rows per sequence over bf16 K/V are a dense
+    // contraction: tensor-core prefill.  Decode rows stay on the split-K
+    // kernel.
+    // (q and out are read and written by TMA there: 16-byte aligned.)
+    if (!b->decode_rows && p->tmap_sw_ok && prefill_tc_supported(p->desc.dtype, D, G, p->desc.block_size) &&
+        (((uintptr_t)q | (uintptr_t)out) & 15) == 0) {
+        PrefillParams pp{};
+        pp.q = q;
+        pp.out = out;
+        pp.table = p->d_table;
+        pp.seqs = b->d_pseqs;
+        pp.n_seqs = b->n_seqs;
+        pp.max_chunks = (b->max_qlen + prefill_queries_per_cta(G) - 1) / prefill_queries_per_cta(G);
+        pp.max_bps = p->max_bps;
+        pp.max_blocks = (int32_t)p->desc.max_blocks;
+        pp.Hq = Hq;
+        pp.Hkv = Hkv;
+        pp.layer = layer;
+        pp.scale_log2 = scale_log2(D);
+        pp.n_rows = b->n_rows;
+        pp.err = p->d_err;
+        if (pp.n_seqs == 0 || pp.max_chunks == 0) return S1KV_OK;
+        return launch_prefill_tc(pp, p->tmap_k_sw, p->tmap_v_sw, stream);
+    }
+    return split_k_attention(b, layer, q, out, Hq, nullptr, stream);
+}
+
+int s1kv_batch_attention_exchange(s1kv_batch* b, int32_t layer, const float* q, int32_t Hq, s1kv_exchange* ex,
+                                  int32_t head0, int32_t heads_total, uint32_t epoch, void* stream_) {
+    if (!b || !ex) return set_error(S1KV_EINVAL, "null batch or exchange");
+    s1kv_pool* p = b->pool;
+    int st = check_layer(p, layer);
+    if (st) return st;
+    if (ex->device != p->device) return set_error(S1KV_EINVAL, "exchange and pool are on different devices");
+    S1KV_ON_DEVICE(p->device);
+    const int32_t Hkv = p->desc.num_kv_heads, D = p->desc.head_dim;
+    if (Hq <= 0 || Hq % Hkv) return set_error(S1KV_EINVAL, "n_q_heads must be a multiple of num_kv_heads");
+    const int G = Hq / Hkv;
+    if (!b->decode_rows || !q) return set_error(S1KV_EINVAL, "exchange: decode batches only (one query row per sequence)");
+    if (!p->tmap_ok || !(decode_mma_supported(p->desc.dtype, D, G, p->desc.block_size) ||
+                         tma_attention_supported(p->desc.dtype, D, G, p->desc.block_size)))
+        return set_error(S1KV_EINVAL, "exchange: shape not served by the split-K decode kernels");
+    if (head0 < 0 || head0 + Hq > heads_total || (int64_t)b->n_rows * heads_total * D > ex->slot_floats)
+        return set_error(S1KV_EINVAL, "exchange: rows x heads x head_dim exceed the exchange slot");
+    AttnParams ex_p{};
+    st = exchange_params(ex, epoch, head0, heads_total, &ex_p);
+    if (st) return st;
+    if (b->n_rows == 0) return S1KV_OK;
+    return split_k_attention(b, layer, q, ex_p.out, Hq, &ex_p, (cudaStream_t)stream_);
 }
 
 int s1kv_batch_layer_host(s1kv_batch* b, int32_t layer, const float* h_q, const float* h_k, const float* h_v,

@@ -462,7 +462,7 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, 
             O = fmaf(mo[(w * NV + g) * D + d], f, O);
         }
         if (rm.n_split == 1) {
-            p.out[((int64_t)item.row * p.Hq + h * G + g) * D + d] = O / L;
+            store_out(p, item.row, h * G + g, d, D, O / L);
         } else {
             p.part_o[(part * G + g) * D + d] = O;
             if (d == 0) {
@@ -471,6 +471,7 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, 
             }
         }
     }
+    if (rm.n_split == 1) signal_done(p);
     if (p.counters && rm.n_split > 1)
         finish_split_row(p, item.row, h, rm.n_split, G, D,
                          reinterpret_cast<int*>(smem + C::kRing + NW * C::kPFloats * 4 + NW * NS * 8),

@@ -6,6 +6,33 @@
 
 namespace s1kv {
 
+// Stores element d of (row, local head `head`) of the attention output, and
+// the same element of every peer's buffer (NVLink stores).
+__device__ __forceinline__ void store_out(const AttnParams& p, int64_t row, int head, int d, int D, float v) {
+    const int64_t i = (row * (p.out_stride > 0 ? p.out_stride : p.Hq) + p.out_head0 + head) * D + d;
+    p.out[i] = v;
+    for (int k = 0; k < p.n_peers; k++) p.peer_out[k][i] = v;
+}
+
+// Called by every thread of a CTA that has just stored a finished (row, KV
+// head): when the launch's last such CTA arrives, this rank's flag on every
+// rank is set to the epoch (release, system scope), after every store of the
+// launch (each CTA fences before arriving).
+__device__ __forceinline__ void signal_done(const AttnParams& p) {
+    if (!p.done) return;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t prev = atomicAdd(p.done, 1u);
+        if (prev == (uint32_t)p.done_total - 1) {
+            *p.done = 0;
+            __threadfence_system();
+            for (int r = 0; r < p.n_flags; r++)
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.flag_dst[r]), "r"(p.epoch) : "memory");
+        }
+    }
+}
+
 // out[row, h*G + g, :] = sum_s 2^(M_s - M) O_s / sum_s 2^(M_s - M) L_s over
 // the n_split partials (max M_s in log2 units, sum L_s, unnormalised O_s)
 // of query row `row` and KV head h; run by `nthreads` threads of one CTA.
@@ -29,7 +56,7 @@ __device__ __forceinline__ void combine_partials(const AttnParams& p, int row, i
             L = fmaf(__ldcg(&p.part_ml[(part * G + g) * 2 + 1]), f, L);
             O = fmaf(__ldcg(&p.part_o[(part * G + g) * D + d]), f, O);
         }
-        p.out[((int64_t)row * p.Hq + h * G + g) * D + d] = O / L;
+        store_out(p, row, h * G + g, d, D, O / L);
     }
 }
 
@@ -82,7 +109,7 @@ __device__ __forceinline__ void combine_partials_staged(const AttnParams& p, int
         }
         for (; s < ns; s++) acc[0] = fmaf(__ldcg(po + s * stride), w[s * G + g], acc[0]);
         const float O = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
-        p.out[((int64_t)row * p.Hq + h * G + g) * D + d] = O * mg[g];
+        store_out(p, row, h * G + g, d, D, O * mg[g]);
     }
 }
 
@@ -108,6 +135,7 @@ __device__ __forceinline__ void finish_split_row(const AttnParams& p, int row, i
         else
             combine_partials(p, row, h, G, D, threadIdx.x, blockDim.x);
         if (threadIdx.x == 0) p.counters[(int64_t)row * p.Hkv + h] = 0;
+        signal_done(p);
     }
 }
 

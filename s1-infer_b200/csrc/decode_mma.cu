@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
             O = fmaf(mo[(w * G + g) * kD + d], f, O);
         }
         if (rm.n_split == 1) {
-            p.out[((int64_t)item.row * p.Hq + h * G + g) * kD + d] = O / L;
+            store_out(p, item.row, h * G + g, d, kD, O / L);
         } else {
             p.part_o[(part * G + g) * kD + d] = O;
             if (d == 0) {
@@ -333,6 +333,7 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
             }
         }
     }
+    if (rm.n_split == 1) signal_done(p);
     if (p.counters && rm.n_split > 1)
         finish_split_row(p, item.row, h, rm.n_split, G, kD, reinterpret_cast<int*>(smem + kRing + kNW * kNS * 8),
                          reinterpret_cast<float*>(smem), kRing / 4);  // the rings are free by now

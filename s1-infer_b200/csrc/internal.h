@@ -95,6 +95,18 @@ struct AttnParams {
     int* err;
     int32_t* counters;     // [n_rows][Hkv] arrivals of split CTAs, zero between launches;
                            // NULL = partials are merged by a separate combine launch
+    // Output placement and the optional exchange of finished rows with peer
+    // GPUs (KV-head sharding): row r, local head j goes to
+    // out[(r * out_stride + out_head0 + j) * D + d] (out_stride 0 = Hq) and
+    // the same element of every peer_out buffer.
+    int32_t out_stride, out_head0;
+    int32_t n_peers;
+    float* peer_out[7];
+    uint32_t* done;        // completion count of this launch's finished rows (NULL: no signal)
+    int32_t done_total;    // rows x KV heads
+    int32_t n_flags;
+    uint32_t* flag_dst[8]; // this rank's flag on every rank (self included)
+    uint32_t epoch;
 };
 
 // One sequence of a prefill batch (tensor-core prefill kernel).
@@ -245,6 +257,16 @@ struct s1kv_pool {
     cudaEvent_t io_ev[4] = {nullptr, nullptr, nullptr, nullptr};
 };
 
+// Peer exchange of attention outputs for KV-head sharding (exchange.cu).
+struct s1kv_exchange {
+    int device = 0, rank = 0, world = 1;
+    int64_t slot_floats = 0;          // one layer's gathered output [B][Hq_total][D]
+    char* base = nullptr;             // [2 slots][slot_floats] floats, then flags[2][8], then done counter
+    char* peer_base[8] = {};          // other ranks' bases (IPC), NULL for self
+    bool opened = false;
+    int* d_err = nullptr;
+};
+
 struct s1kv_batch {
     s1kv_pool* pool = nullptr;
     s1kv::StageSeg* seg = nullptr;
@@ -309,6 +331,9 @@ int launch_decode_with_maps(const AttnParams& p, const CUtensorMap& tk, const CU
 // partials in the same format as the CUDA-core decode kernel.
 bool decode_mma_supported(int dtype, int D, int G, int block_size);
 int launch_decode_mma(const AttnParams& p, const CUtensorMap& tk_sw, const CUtensorMap& tv_sw, cudaStream_t stream);
+
+// Exchange fields of a decode launch that publishes its rows (exchange.cu).
+int exchange_params(const s1kv_exchange* ex, uint32_t epoch, int32_t head0, int32_t heads_total, AttnParams* ap);
 
 // Tensor-core prefix-hit prefill (prefill_tc.cu).
 bool prefill_tc_supported(int dtype, int D, int G, int block_size);

@@ -110,6 +110,13 @@ SIGNATURES = {
     "s1kv_prefix_save_v1": (C.c_int, [vp, u64, P(i32), C.c_char_p]),
     "s1kv_prefix_file_info": (C.c_int, [C.c_char_p, vp]),
     "s1kv_prefix_load_v1": (C.c_int, [vp, u64, C.c_char_p, i32, P(i64)]),
+    "s1kv_exchange_create": (C.c_int, [C.c_int, i32, i32, i64, P(vp)]),
+    "s1kv_exchange_handle": (C.c_int, [vp, vp]),
+    "s1kv_exchange_open": (C.c_int, [vp, vp]),
+    "s1kv_exchange_buffer": (vp, [vp, C.c_uint32]),
+    "s1kv_exchange_wait": (C.c_int, [vp, C.c_uint32, vp]),
+    "s1kv_exchange_destroy": (C.c_int, [vp]),
+    "s1kv_batch_attention_exchange": (C.c_int, [vp, i32, vp, i32, vp, i32, i32, C.c_uint32, vp]),
     "s1kv_batch_norm_rope_append": (C.c_int, [vp, i32, vp, vp, i32, vp, vp, vp, vp, f32, vp]),
     "s1kv_debug_div_check": (C.c_int, [vp, i64, vp, i64, vp, vp]),
     "s1kv_batch_append": (C.c_int, [vp, i32, vp, vp, vp]),
@@ -567,3 +574,62 @@ def gather_heads(out_local, world, group=None, buf=None):
     else:
         dist.all_gather(list(buf.unbind(0)), src, group=group)
     return buf.transpose(0, 1).reshape(B, world * hq_l, D)
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ view of device memory owned elsewhere."""
+
+    def __init__(self, ptr, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class PeerExchange:
+    """Fused output exchange of a KV-head-sharded job (s1kv_exchange_*): the
+    decode kernels store each finished row into every rank's token-major
+    buffer [rows, heads_total, head_dim] over NVLink and signal the layer's
+    epoch; wait(epoch) makes the stream wait (bounded) for all ranks.  The
+    CUDA IPC handles are exchanged once through torch.distributed."""
+
+    def __init__(self, rank, world, rows, heads_total, head_dim, device=None, group=None):
+        import torch
+        self.L = lib()
+        self.rank, self.world = rank, world
+        self.shape = (rows, heads_total, head_dim)
+        dev = torch.cuda.current_device() if device is None else device
+        h = vp()
+        check(self.L.s1kv_exchange_create(dev, rank, world, rows * heads_total * head_dim, C.byref(h)))
+        self.h = h
+        if world > 1:
+            import torch.distributed as dist
+            mine = (C.c_char * 64)()
+            check(self.L.s1kv_exchange_handle(h, mine))
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(mine), group=group)
+            arr = (C.c_char * (64 * world)).from_buffer_copy(b"".join(handles))
+            check(self.L.s1kv_exchange_open(h, arr))
+
+    def attention(self, batch, layer, q, head0, epoch):
+        """Decode attention of this rank's query heads q [rows, Hq_local, D]
+        (global heads head0 ..), published under `epoch`."""
+        check(self.L.s1kv_batch_attention_exchange(batch.h, layer, _dptr(q), q.shape[1], self.h, head0, self.shape[1],
+                                                   epoch, _stream()))
+
+    def wait(self, epoch):
+        check(self.L.s1kv_exchange_wait(self.h, epoch, _stream()))
+
+    def output(self, epoch, rows=None):
+        """The gathered [rows, heads_total, head_dim] of `epoch` (a view of
+        the exchange's memory; valid until the slot is reused two epochs
+        later or the exchange is closed)."""
+        import torch
+        ptr = self.L.s1kv_exchange_buffer(self.h, epoch)
+        t = torch.as_tensor(_DeviceArray(ptr, self.shape), device="cuda")
+        return t if rows is None else t[:rows]
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.s1kv_exchange_destroy(self.h)
+            self.h = None
+
+    __del__ = close
