@@ -548,6 +548,7 @@ def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3):
         xchg_ms = float(np.mean([evs[i][l][1].elapsed_time(evs[i][l][2]) for i in range(steps) for l in range(layers)]))
         res[mode] = (elapsed, max_over_ranks(torch, world, attn_ms), max_over_ranks(torch, world, xchg_ms), ctx_before)
     s1kv.device_check(torch.cuda.current_device())
+    barrier(torch, world)  # no rank frees its exchange buffer while a peer may still hold it open
     ex.close()
     elapsed, attn_ms, gather_ms, ctx_before = res["fused"]
     # algorithmic bytes of one layer's attention on this GPU: K and V of the

@@ -113,6 +113,7 @@ def _rank_fused(rank, world, port, out_dir):
             outs.append(ex.output(e).clone())
     torch.cuda.synchronize()
     assert pool.check_device() == 0
+    dist.barrier()  # no rank frees its buffer while a peer may still hold it open
     ex.close()
     pool.close()
     dist.barrier()
