@@ -615,8 +615,12 @@ class PeerExchange:
         check(self.L.s1kv_batch_attention_exchange(batch.h, layer, _dptr(q), q.shape[1], self.h, head0, self.shape[1],
                                                    epoch, _stream()))
 
-    def wait(self, epoch):
-        check(self.L.s1kv_exchange_wait(self.h, epoch, _stream()))
+    def wait(self, epoch, force=False):
+        """Makes the stream wait until every rank signalled `epoch`.  With one
+        rank the stream order already covers it, so nothing is launched
+        unless `force`."""
+        if self.world > 1 or force:
+            check(self.L.s1kv_exchange_wait(self.h, epoch, _stream()))
 
     def output(self, epoch, rows=None):
         """The gathered [rows, heads_total, head_dim] of `epoch` (a view of

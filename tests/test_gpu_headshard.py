@@ -156,7 +156,7 @@ def test_exchange_wait_times_out_on_a_flag_nobody_sets(cuda):
     sys.path.insert(0, os.path.join(ROOT, "s1-infer_b200"))
     import s1kv
     ex = s1kv.PeerExchange(0, 1, 2, 8, 64)
-    ex.wait(7)
+    ex.wait(7, force=True)
     torch.cuda.synchronize()
     with pytest.raises(s1kv.S1KVError) as e:
         s1kv.device_check(torch.cuda.current_device())
