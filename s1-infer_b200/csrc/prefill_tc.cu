@@ -301,9 +301,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        for (int i = 0; i < kNumBars; i++) bar_init(&bars[i], 1);
-        bar_init(&p_full[0], 4);  // one arrive per softmax warp
-        bar_init(&p_full[1], 4);
+        // each barrier initialised once; p_full takes one arrive per softmax warp
+        for (int i = 0; i < kNumBars; i++) bar_init(&bars[i], (i == 4 * kStages + 2 || i == 4 * kStages + 3) ? 4u : 1u);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         // both query tiles, fp32, rows (query, head) query-major; rows past
