@@ -18,7 +18,7 @@
 //     TMA (one 16-row x 64-element box per block and 128-byte half of a
 //     row, 128B swizzle, no multicast), issued by 16 lanes of the producer
 //     warp in parallel into a 2-stage ring; completion on mbarriers.
-//   * One thread of the MMA warp issues S_X = Q_X K^T (M 128, N 128, K 128)
+//   * The MMA warp (one elected lane) issues S_X = Q_X K^T (M 128, N 128, K 128)
 //     and O_X += P_X V (M 128, N 128, K 128, A read from TMEM) as
 //     tcgen05.mma kind::f16 with fp32 accumulators in TMEM (512 columns:
 //     S_A, S_B, O_A, O_B).  Order PV_A(t) S_A(t+1) PV_B(t) S_B(t+1): a
@@ -56,7 +56,6 @@ constexpr int kThreads = kSoftmaxThreads + 64;  // + TMA warp + MMA warp
 constexpr int kTmemCols = 512;   // S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512)
 constexpr int kColO = 256;
 constexpr float kRescaleAt = 8.0f;  // log2 units: O is rescaled only when a row max grows by > 2^8
-
 // shared memory layout (bytes, 1024-aligned pieces)
 constexpr int kQBytes = 2 * kM * 128;          // one query tile: 2 atoms x 128 rows x 128 B = 32 KB
 constexpr int kKBytes = 2 * kN * 128;          // 2 d-atoms x 128 tokens x 128 B = 32 KB
@@ -88,6 +87,17 @@ __device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t phase) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+// Non-blocking probe of a phase (mbarrier.test_wait); the waits below try it
+// before the potentially suspending try_wait.
+__device__ __forceinline__ bool bar_test(uint64_t* b, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
         : "r"(su32(b)), "r"(phase)
         : "memory");
@@ -139,25 +149,30 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn_major, 
            ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// MMAs and commits are run by a whole warp, one elected lane issuing: the
+// issuing warp stays converged, so its operands never leave the warp-uniform
+// path.
 // D (TMEM) (+)= A (shared) * B (shared)
-__device__ __forceinline__ void mma_ss(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, bool accumulate) {
+__device__ __forceinline__ void mma_ss_w(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, bool accumulate) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "{\n\t.reg .pred e, p;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(a), "l"(b), "r"(idesc), "r"((uint32_t)accumulate)
         : "memory");
 }
 // D (TMEM) (+)= A (TMEM) * B (shared)
-__device__ __forceinline__ void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, bool accumulate) {
+__device__ __forceinline__ void mma_ts_w(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, bool accumulate) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "{\n\t.reg .pred e, p;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
         "r"(tmem_a), "l"(b), "r"(idesc), "r"((uint32_t)accumulate)
         : "memory");
 }
-__device__ __forceinline__ void mma_commit(uint64_t* b) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b))
-                 : "memory");
+__device__ __forceinline__ void mma_commit_w(uint64_t* b) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(su32(b))
+        : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -231,6 +246,7 @@ __device__ __forceinline__ float ex2f(float x) {
     return y;
 }
 
+
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -243,6 +259,7 @@ __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 12
 // Bounded wait that also gives up when another role of the CTA raised the
 // abort flag; a timeout raises it.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* b, uint32_t phase, volatile int* abort_flag) {
+    if (bar_test(b, phase)) return true;
     for (uint32_t i = 0; i < kSpin; i++) {
         if (bar_try(b, phase)) return true;
         if (*abort_flag) return false;
@@ -369,64 +386,74 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = max(0, v_issued - kStages); t < v_issued; t++) bar_wait(&v_full[t % kStages], (uint32_t)((t / kStages) & 1));
     } else if (warp == kSoftmaxThreads / 32 + 1) {
         // ================= MMA issuer =================
-        if (lane == 0) {
+        // The whole warp runs the loop and its waits; one elected lane issues
+        // each MMA and commit.
+        {
             constexpr uint32_t idS = idesc_bf16(kM, kN, 0, 0);  // Q, K both K-major
             constexpr uint32_t idO = idesc_bf16(kM, kD, 0, 1);  // P from TMEM, V MN-major
-            const uint32_t qa[2] = {su32(smem + kOffQ), su32(smem + kOffQ + kQBytes)};
+            // Descriptors of every operand buffer, built once.  The start
+            // address is the descriptor's low field (address / 16, 14 bits;
+            // shared addresses stay below 2^18), so a K step's offset inside a
+            // buffer is a constant added to the buffer's descriptor and the
+            // issue loops below are the MMAs alone.
+            static_assert(kStages == 2, "descriptors are selected by tile parity");
+            const uint64_t dq0 = sdesc(su32(smem + kOffQ), 16, 1024), dq1 = sdesc(su32(smem + kOffQ + kQBytes), 16, 1024);
+            const uint64_t dk0 = sdesc(su32(smem + kOffK), 16, 1024), dk1 = sdesc(su32(smem + kOffK + kKBytes), 16, 1024);
+            const uint64_t dv0 = sdesc(su32(smem + kOffV), kN * 128, 1024);
+            const uint64_t dv1 = sdesc(su32(smem + kOffV + kVBytes), kN * 128, 1024);
             auto issue_s = [&](int X, int t) {
-                const uint32_t ka = su32(smem + kOffK + (t % kStages) * kKBytes);
+                const uint64_t da = X ? dq1 : dq0, db = (t & 1) ? dk1 : dk0;
 #pragma unroll
                 for (int ks = 0; ks < kD / 16; ks++) {
-                    const uint32_t off = (ks & 3) * 32;  // 16 elements = 32 bytes inside a 128-byte atom row
-                    const uint64_t da = sdesc(qa[X] + (ks >> 2) * (kM * 128) + off, 16, 1024);
-                    const uint64_t db = sdesc(ka + (ks >> 2) * (kN * 128) + off, 16, 1024);
-                    mma_ss(tmem + X * 128, da, db, idS, ks > 0);
+                    // 16 elements = 32 bytes inside a 128-byte atom row; 64 elements per atom column
+                    constexpr uint32_t kAtomA = kM * 128 / 16, kAtomB = kN * 128 / 16;
+                    mma_ss_w(tmem + X * 128, da + (ks >> 2) * kAtomA + (ks & 3) * 2, db + (ks >> 2) * kAtomB + (ks & 3) * 2,
+                           idS, ks > 0);
                 }
-                mma_commit(&s_full[X]);
+                mma_commit_w(&s_full[X]);
             };
             auto issue_pv = [&](int X, int t) {
-                const uint32_t va = su32(smem + kOffV + (t % kStages) * kVBytes);
+                const uint64_t db = (t & 1) ? dv1 : dv0;
 #pragma unroll
                 for (int ks = 0; ks < kN / 16; ks++) {
                     // P: 16 tokens = 8 columns of bf16 pairs; V: 16 token rows = 2 KB
-                    const uint64_t db = sdesc(va + ks * 16 * 128, kN * 128, 1024);
-                    mma_ts(tmem + kColO + X * 128, tmem + X * 128 + ks * 8, db, idO, t > 0 || ks > 0);
+                    mma_ts_w(tmem + kColO + X * 128, tmem + X * 128 + ks * 8, db + ks * (16 * 128 / 16), idO, t > 0 || ks > 0);
                 }
-                mma_commit(&pv_done[X]);
+                mma_commit_w(&pv_done[X]);
             };
-            bool ok = wait_or_abort(&k_full[0], 0, abort_flag);
+            bool ok = warp_wait(&k_full[0], 0, abort_flag);
             if (ok) {
                 tc_fence_after();
                 issue_s(0, 0);
                 issue_s(1, 0);
-                mma_commit(&k_empty[0]);
+                mma_commit_w(&k_empty[0]);
             }
             for (int t = 0; t < n_tiles && ok; t++) {
                 const int slot = t % kStages;
                 const bool more = t + 1 < n_tiles;
                 const int ns = (t + 1) % kStages;
-                ok = wait_or_abort(&p_full[0], (uint32_t)(t & 1), abort_flag) &&
-                     wait_or_abort(&v_full[slot], (uint32_t)((t / kStages) & 1), abort_flag);
+                ok = warp_wait(&p_full[0], (uint32_t)(t & 1), abort_flag) &&
+                     warp_wait(&v_full[slot], (uint32_t)((t / kStages) & 1), abort_flag);
                 if (!ok) break;
                 tc_fence_after();
                 issue_pv(0, t);
                 if (more) {  // S_A(t+1) overwrites P_A(t): issued after PV_A(t), which reads it first
-                    ok = wait_or_abort(&k_full[ns], (uint32_t)(((t + 1) / kStages) & 1), abort_flag);
+                    ok = warp_wait(&k_full[ns], (uint32_t)(((t + 1) / kStages) & 1), abort_flag);
                     if (!ok) break;
                     issue_s(0, t + 1);
                 }
-                ok = wait_or_abort(&p_full[1], (uint32_t)(t & 1), abort_flag);
+                ok = warp_wait(&p_full[1], (uint32_t)(t & 1), abort_flag);
                 if (!ok) break;
                 tc_fence_after();
                 issue_pv(1, t);
-                mma_commit(&v_empty[slot]);
+                mma_commit_w(&v_empty[slot]);
                 if (more) {
                     issue_s(1, t + 1);
-                    mma_commit(&k_empty[ns]);
+                    mma_commit_w(&k_empty[ns]);
                 }
             }
-            // everything this thread issued has finished before TMEM is freed
-            mma_commit(drain);
+            // everything this warp issued has finished before TMEM is freed
+            mma_commit_w(drain);
             bar_wait(drain, 0);
         }
     } else {
