@@ -64,8 +64,9 @@ constexpr int kOffQ = 0;                        // Q_A, Q_B
 constexpr int kOffK = kOffQ + 2 * kQBytes;      // K ring
 constexpr int kOffV = kOffK + kStages * kKBytes;  // V ring
 constexpr int kOffBar = kOffV + kStages * kVBytes;
-// barriers: k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], pv_done[2], drain, q_full
-constexpr int kNumBars = 4 * kStages + 8;
+// barriers: k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], pv_done[2], drain, q_full,
+// p_lo[2]
+constexpr int kNumBars = 4 * kStages + 10;
 // Q arrives as fp32 by TMA into the (still idle) K/V ring: one box of
 // 128 (query, head) rows x 512 bytes per query tile
 constexpr int kQStageBytes = kM * kD * 4;
@@ -295,6 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* pv_done = bars + 4 * kStages + 4;  // [2]
     uint64_t* drain = bars + 4 * kStages + 6;
     uint64_t* q_full = bars + 4 * kStages + 7;
+    uint64_t* p_lo = bars + 4 * kStages + 8;  // [2]: first half of P_X (tokens 0-63) is in TMEM
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
     int32_t* sIds = reinterpret_cast<int32_t*>(smem + kOffIds);
@@ -319,7 +321,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (tid == 0) {
         // each barrier initialised once; p_full takes one arrive per softmax warp
-        for (int i = 0; i < kNumBars; i++) bar_init(&bars[i], (i == 4 * kStages + 2 || i == 4 * kStages + 3) ? 4u : 1u);
+        for (int i = 0; i < kNumBars; i++) {
+            const bool per_warp = i == 4 * kStages + 2 || i == 4 * kStages + 3 || i >= 4 * kStages + 8;  // p_full, p_lo
+            bar_init(&bars[i], per_warp ? 4u : 1u);
+        }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         // both query tiles, fp32, rows (query, head) query-major; rows past
@@ -412,14 +417,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 mma_commit_w(&s_full[X]);
             };
-            auto issue_pv = [&](int X, int t) {
+            // PV in two halves of 64 tokens: the first runs while the softmax
+            // still computes the second half of P
+            auto issue_pv_half = [&](int X, int t, int half) {
                 const uint64_t db = (t & 1) ? dv1 : dv0;
 #pragma unroll
-                for (int ks = 0; ks < kN / 16; ks++) {
+                for (int k = 0; k < kN / 32; k++) {
+                    const int ks = half * (kN / 32) + k;
                     // P: 16 tokens = 8 columns of bf16 pairs; V: 16 token rows = 2 KB
                     mma_ts_w(tmem + kColO + X * 128, tmem + X * 128 + ks * 8, db + ks * (16 * 128 / 16), idO, t > 0 || ks > 0);
                 }
-                mma_commit_w(&pv_done[X]);
+                if (half) mma_commit_w(&pv_done[X]);
             };
             bool ok = warp_wait(&k_full[0], 0, abort_flag);
             if (ok) {
@@ -432,20 +440,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int slot = t % kStages;
                 const bool more = t + 1 < n_tiles;
                 const int ns = (t + 1) % kStages;
-                ok = warp_wait(&p_full[0], (uint32_t)(t & 1), abort_flag) &&
+                ok = warp_wait(&p_lo[0], (uint32_t)(t & 1), abort_flag) &&
                      warp_wait(&v_full[slot], (uint32_t)((t / kStages) & 1), abort_flag);
                 if (!ok) break;
                 tc_fence_after();
-                issue_pv(0, t);
+                issue_pv_half(0, t, 0);
+                ok = warp_wait(&p_full[0], (uint32_t)(t & 1), abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv_half(0, t, 1);
                 if (more) {  // S_A(t+1) overwrites P_A(t): issued after PV_A(t), which reads it first
                     ok = warp_wait(&k_full[ns], (uint32_t)(((t + 1) / kStages) & 1), abort_flag);
                     if (!ok) break;
                     issue_s(0, t + 1);
                 }
+                ok = warp_wait(&p_lo[1], (uint32_t)(t & 1), abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv_half(1, t, 0);
                 ok = warp_wait(&p_full[1], (uint32_t)(t & 1), abort_flag);
                 if (!ok) break;
                 tc_fence_after();
-                issue_pv(1, t);
+                issue_pv_half(1, t, 1);
                 mma_commit_w(&v_empty[slot]);
                 if (more) {
                     issue_s(1, t + 1);
@@ -484,12 +500,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < kN; j++)
                     if (base + j > row_limit) sc[j] = -INFINITY;
             }
-            // Row max of the raw scores over four independent chains; rounding
-            // is monotonic, so max(s) * scale equals max(s * scale) exactly.
-            float m4[4] = {sc[0], sc[1], sc[2], sc[3]};
+            // Row max of the raw scores over eight independent chains (16 deep);
+            // rounding is monotonic, so max(s) * scale equals max(s * scale)
+            // exactly.
+            float m8[8];
 #pragma unroll
-            for (int j = 4; j < kN; j++) m4[j & 3] = fmaxf(m4[j & 3], sc[j]);
-            const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
+            for (int j = 0; j < 8; j++) m8[j] = sc[j];
+#pragma unroll
+            for (int j = 8; j < kN; j++) m8[j & 7] = fmaxf(m8[j & 7], sc[j]);
+            const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) *
+                             p.scale_log2;
             const bool raise = mx > m + kRescaleAt;
             float corr = 1.0f;
             if (raise) {
@@ -501,6 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // p = 2^(s * scale - mref): one packed FFMA per pair, then ex2
             const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-mref, -mref);
             float2 ls2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            const bool rescale = t > 0 && __any_sync(0xffffffffu, raise);  // warp-uniform
 #pragma unroll
             for (int q = 0; q < 4; q++) {
                 float pk[16];
@@ -513,9 +535,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     pk[e] = __uint_as_float(pack_bf16(pv.x, pv.y));
                 }
                 tmem_st16_nowait(tS + q * 16, pk);
+                if (q == 1 && !rescale) {
+                    // first half of P (tokens 0-63) handed over: its PV half
+                    // runs while the second half is computed
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) bar_arrive(&p_lo[X]);
+                }
             }
-            // rescale O_X (the scores are dead by now: no register pressure)
-            if (t > 0 && __any_sync(0xffffffffu, raise)) {
+            // Rescale O_X (the scores are dead by now: no register pressure).
+            // A warp that rescales hands over both halves of P only after it,
+            // since the first PV half accumulates into O.
+            if (rescale) {
 #pragma unroll 1
                 for (int c = 0; c < kD / 32; c++) {
                     float ov[32];
@@ -529,7 +561,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             l += (ls2[0].x + ls2[1].x) + (ls2[0].y + ls2[1].y);
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) bar_arrive(&p_full[X]);
+            if (lane == 0) {
+                if (rescale) bar_arrive(&p_lo[X]);
+                bar_arrive(&p_full[X]);
+            }
         }
         // last PV of this tile, then the output rows
         if (ok && warp_wait(&pv_done[X], (uint32_t)((n_tiles - 1) & 1), abort_flag)) {
