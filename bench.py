@@ -657,6 +657,121 @@ def run_cfg5(s1kv, torch, rank, world, steps=100, warmup=20):
             "evictions_total": st["evictions"], "occupancy": 1.0 - st["num_free"] / max_blocks}
 
 
+# int8 projections of one decode token through the reference's model shape
+# (Qwen3-0.6B: hidden 1024, 16 query heads and 8 KV heads of 128, MLP 3072,
+# 28 layers; src/nn/attention.cpp:253-254, tests/test_layer.cpp:20-27) with
+# the Qwen3 vocabulary for the LM head (src/model/model.cpp:177).
+INT8_LAYERS, INT8_VOCAB = 28, 151936
+INT8_PROJ = [("q_proj", 1024, 2048), ("k_proj", 1024, 1024), ("v_proj", 1024, 1024), ("o_proj", 2048, 1024),
+             ("gate_proj", 1024, 3072), ("up_proj", 1024, 3072), ("down_proj", 3072, 1024)]
+
+
+def run_int8(s1kv, torch, rank, steps=20, warmup=3, cpu_sample=True):
+    """The int8 projections either side of the KV path for one decode step:
+    28 layers x 7 weights plus the LM head [1024, 151936], quantized with
+    quantize_tensor (one scale per row), multiplied by M = 1 (the
+    reference's single-sequence decode) and M = 8 rows.  596 MB of int8
+    weights, far above L2: every step streams them from HBM.  A step's 197
+    launches are captured once in a CUDA graph and replayed; the LM head is
+    also timed alone (155.6 MB per launch).  Roofline: weight bytes (+ x and
+    out) per step over the measured HBM copy bandwidth."""
+    gen = torch.Generator(device="cuda").manual_seed(31 + rank)
+    mats = []
+    for _ in range(INT8_LAYERS):
+        for _, K, N in INT8_PROJ:
+            mats.append(s1kv.quantize_tensor(torch.randn((K, N), device="cuda", generator=gen) * 0.05))
+    w = torch.randn((1024, INT8_VOCAB), device="cuda", generator=gen) * 0.05
+    mats.append(s1kv.quantize_tensor(w))
+    del w
+    torch.cuda.synchronize()
+    wbytes = sum(q.rows * q.cols + 4 * q.rows for q in mats)
+    peak, _ = load_peaks()
+    res = {}
+    for M in (1, 8):
+        xs = {K: torch.randn((M, K), device="cuda", generator=gen) for K in (1024, 2048, 3072)}
+        outs = [torch.empty((M, q.cols), device="cuda") for q in mats]
+
+        def step(sel=None):
+            for qt, o in (zip(mats, outs) if sel is None else [sel]):
+                s1kv.matmul_quantized(xs[qt.rows], qt, out=o)
+
+        step()  # first launches (attributes, cluster query) outside the capture
+        torch.cuda.synchronize()
+        l0 = s1kv.launch_count()
+        g, gl = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        with torch.cuda.graph(gl):
+            step((mats[-1], outs[-1]))
+        launches = s1kv.launch_count() - l0 - 1
+        io_bytes = sum(4 * M * (q.rows + q.cols) for q in mats)
+        times = {}
+        for name, gr in (("step", g), ("lm_head", gl)):
+            for _ in range(warmup):
+                gr.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(steps):
+                gr.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            times[name] = e0.elapsed_time(e1) / steps
+        # end to end: x from pinned host memory, the LM-head logits back
+        hx = torch.randn((M, 1024), generator=torch.Generator().manual_seed(7)).pin_memory()
+        hout = torch.empty((M, INT8_VOCAB)).pin_memory()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            xs[1024].copy_(hx, non_blocking=True)
+            g.replay()
+            hout.copy_(outs[-1], non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / steps
+        lm = mats[-1]
+        lm_bytes = lm.rows * lm.cols + 4 * lm.rows + 4 * M * (lm.rows + lm.cols)
+        res[f"M{M}"] = {
+            "ms_per_step": times["step"], "tok_s": M / (times["step"] * 1e-3),
+            "weight_gbs": (wbytes + io_bytes) / (times["step"] * 1e-3) / 1e9,
+            "frac_of_hbm": (wbytes + io_bytes) / (times["step"] * 1e-3) / 1e9 / peak,
+            "launches_per_step": launches,
+            "lm_head_ms": times["lm_head"], "lm_head_gbs": lm_bytes / (times["lm_head"] * 1e-3) / 1e9,
+            "lm_head_frac_of_hbm": lm_bytes / (times["lm_head"] * 1e-3) / 1e9 / peak,
+            "e2e_ms_per_step": e2e_ms, "e2e_tok_s": M / (e2e_ms * 1e-3),
+            "e2e_h2d_bytes_per_step": 4 * M * 1024, "e2e_d2h_bytes_per_step": 4 * M * INT8_VOCAB}
+        del g, gl
+    out = {"workload": f"int8 projections of one decode step: {INT8_LAYERS} layers x (q 1024x2048, k/v 1024x1024, "
+                       f"o 2048x1024, gate/up 1024x3072, down 3072x1024) + LM head 1024x{INT8_VOCAB}, one scale "
+                       f"per row, seeded normal weights",
+           "weight_bytes_per_step": wbytes, "l2": "weights 596 MB per step, above L2", **res}
+    if cpu_sample and rank == 0:
+        from oracle import oracle as O
+        if O.ref_available():
+            import time as _t
+            layer = mats[:len(INT8_PROJ)]
+            host = [(q.data.cpu().numpy(), q.scales.cpu().numpy()) for q in layer + [mats[-1]]]
+            x1 = {K: np.random.default_rng(K).standard_normal((1, K)).astype(np.float32) for K in (1024, 2048, 3072)}
+            best = {}
+            for _ in range(2):
+                t0 = _t.perf_counter()
+                for q, sc in host[:-1]:
+                    O.ref_matmul_int8(x1[q.shape[0]], q, sc, threaded=True)
+                t1 = _t.perf_counter()
+                O.ref_matmul_int8(x1[1024], host[-1][0], host[-1][1], threaded=True)
+                t2 = _t.perf_counter()
+                best["layer"] = min(best.get("layer", 1e9), t1 - t0)
+                best["lm"] = min(best.get("lm", 1e9), t2 - t1)
+            tok_ms = (best["layer"] * INT8_LAYERS + best["lm"]) * 1e3
+            out["cpu_baseline"] = {"value": 1e3 / tok_ms, "unit": "tok/s (M = 1)", "cores": os.cpu_count() or 1,
+                                   "kind": "reference",
+                                   "sample": "matmul_quantized (thread pool) on layer 0's 7 weights (x28) and the LM "
+                                             "head, M = 1, best of 2",
+                                   "ms_per_step": tok_ms,
+                                   "weight_gbs": wbytes / (tok_ms * 1e-3) / 1e9}
+    return out
+
+
 def run_ours(args):
     import torch
     import s1kv
@@ -680,10 +795,13 @@ def run_ours(args):
     cfg3 = run_cfg3(s1kv, torch, rank, n=args.cfg3_seqs) if not args.only or args.only == "cfg3" else None
     cfg4 = run_cfg4(s1kv, torch, rank, world) if not args.only or args.only == "cfg4" else None
     cfg5 = run_cfg5(s1kv, torch, rank, world) if not args.only or args.only == "cfg5" else None
+    int8 = run_int8(s1kv, torch, rank, cpu_sample=(world == 1 and not args.no_cpu_baseline)) \
+        if not args.only or args.only == "int8" else None
     if args.only:
         # profiling case: one variant, no summary line
-        if rank == 0 and args.only in ("cfg3", "cfg4", "cfg5"):
-            print(json.dumps({"profiling_case": args.only, **{"cfg3": cfg3, "cfg4": cfg4, "cfg5": cfg5}[args.only]}))
+        if rank == 0 and args.only in ("cfg3", "cfg4", "cfg5", "int8"):
+            print(json.dumps({"profiling_case": args.only,
+                              **{"cfg3": cfg3, "cfg4": cfg4, "cfg5": cfg5, "int8": int8}[args.only]}))
         elif rank == 0:
             r = res[args.only]
             print(json.dumps({"profiling_case": args.only, "layers": LAYERS, "ms_per_step": r["elapsed_ms"] / args.steps,
@@ -766,7 +884,11 @@ def run_ours(args):
             "cfg4_head_sharded": None if cfg4 is None else {
                 **cfg4, "roofline": {"bound": "hbm", "achieved": cfg4["kv_gbs_per_gpu"], "peak": peak,
                                      "frac": cfg4["kv_gbs_per_gpu"] / peak, "unit": "GB/s"}},
-            "cfg5_churn": cfg5},
+            "cfg5_churn": cfg5,
+            "int8_projections": None if int8 is None else {
+                **int8, "roofline": {"bound": "hbm", "achieved": int8["M1"]["weight_gbs"], "peak": peak,
+                                     "frac": int8["M1"]["frac_of_hbm"], "unit": "GB/s",
+                                     "lm_head_alone_frac": int8["M1"]["lm_head_frac_of_hbm"]}}},
         "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
     }
     print(json.dumps(line))
@@ -833,7 +955,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling cases only (the bench line uses 32)")
-    ap.add_argument("--only", choices=["f32", "bf16", "cfg3", "cfg4", "cfg5"], help="profiling case: run one variant")
+    ap.add_argument("--only", choices=["f32", "bf16", "cfg3", "cfg4", "cfg5", "int8"],
+                    help="profiling case: run one variant")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cfg3-seqs", type=int, default=256, help="profiling case: sequences of the cfg3 variant")
     args = ap.parse_args()

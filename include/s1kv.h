@@ -366,6 +366,29 @@ int s1kv_batch_layer_host(s1kv_batch* batch, int32_t layer, const float* h_q, co
                           float* h_out, int32_t n_q_heads, void* stream);
 int s1kv_batch_end(s1kv_batch* batch, void* stream);
 
+/* ============ int8 projections either side of the KV path ============ */
+/* The reference quantizes every pre-transposed [K, N] weight (the q/k/v
+ * projections whose outputs the append consumes, o_proj after the attention,
+ * the MLP and the LM head) and multiplies with it on the CPU
+ * (src/quantized_tensor.cpp; weights pre-transposed by
+ * src/model/model.cpp:8-33).  Device pointers; asynchronous on `stream`. */
+
+/* quantize_tensor (src/quantized_tensor.cpp:9-47, include/core/
+ * quantized_tensor.h:13): w [rows][cols] fp32 -> q [rows][cols] int8 and
+ * one scale per row, scale = max|w[row,:]| / 127 (1 for an all-zero row),
+ * q = round(w / scale) with ties away from zero.  Bit-exact with the
+ * reference. */
+int s1kv_quantize_rows(const float* w, int64_t rows, int64_t cols, int8_t* q, float* scales, void* stream);
+
+/* matmul_quantized (src/quantized_tensor.cpp:102-122, kernel
+ * matmul_quantized_range_blocked :60-100; include/core/quantized_tensor.h:
+ * 17-23): out [M][N] = x [M][K] * (q [K][N] scaled by scales[k] per row k),
+ * fp32.  Sums over k in a fixed tree order (the same on every run), within
+ * 2e-5 of the output scale of the reference's sequential sum.  K <= 8192;
+ * M any (rows of x are taken 8 at a time). */
+int s1kv_matmul_int8(const float* x, int64_t M, int64_t K, const int8_t* q, const float* scales, int64_t N,
+                     float* out, void* stream);
+
 /* ======================== introspection ======================== */
 
 /* Number of kernel launches this library issued on the calling process

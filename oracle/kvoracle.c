@@ -611,3 +611,38 @@ int kvo_prefix_match(kvo_pool* p, uint64_t dst, const int32_t* tokens, int64_t n
     *n_hit = hit * p->bs;
     return KVO_OK;
 }
+
+/* ======================= int8 projections ======================= */
+
+/* quantize_tensor (src/quantized_tensor.cpp:9-47): per row, scale =
+ * max|w| / 127 (1 when the row is all zero), q = round(w / scale) with
+ * ties away from zero (std::round), cast to int8. */
+void kvo_quantize_rows(const float* w, int64_t rows, int64_t cols, int8_t* q, float* scales) {
+    for (int64_t r = 0; r < rows; r++) {
+        float mx = 0.0f;
+        for (int64_t c = 0; c < cols; c++) {
+            float a = fabsf(w[r * cols + c]);
+            mx = (mx < a) ? a : mx; /* std::max(row_max, |val|), NaN included */
+        }
+        float scale = (mx > 0.0f) ? mx / 127.0f : 1.0f;
+        scales[r] = scale;
+        for (int64_t c = 0; c < cols; c++) q[r * cols + c] = (int8_t)roundf(w[r * cols + c] / scale);
+    }
+}
+
+/* matmul_quantized_range_blocked (src/quantized_tensor.cpp:60-100) over all
+ * columns: out[i][j] = sum over k in order of x[i][k] * (q[k][j] * s[k]),
+ * each product and sum rounded to fp32 on its own (the AVX lanes and the
+ * scalar tail compute the same sequence). */
+void kvo_matmul_int8(const float* x, int64_t M, int64_t K, const int8_t* q, const float* s, int64_t N, float* out) {
+    for (int64_t i = 0; i < M; i++)
+        for (int64_t j = 0; j < N; j++) {
+            float sum = 0.0f;
+            for (int64_t k = 0; k < K; k++) {
+                float b = (float)q[k * N + j] * s[k];
+                float prod = x[i * K + k] * b;
+                sum = sum + prod;
+            }
+            out[i * N + j] = sum;
+        }
+}

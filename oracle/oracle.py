@@ -85,6 +85,8 @@ def _load():
                 "kvo_block_hash": (u64, [u64, vp, i64]),
                 "kvo_prefix_insert": (i64, [vp, u64, vp, i64]),
                 "kvo_prefix_match": (C.c_int, [vp, u64, vp, i64, C.POINTER(i64)]),
+                "kvo_quantize_rows": (None, [vp, i64, i64, vp, vp]),
+                "kvo_matmul_int8": (None, [vp, i64, i64, vp, vp, i64, vp]),
             }
             for name, (res, args) in sig.items():
                 fn = getattr(lib, name)
@@ -120,6 +122,11 @@ def _load_ref():
                 "ref_gqa_attention": (None, [vp, vp, vp, i64, i64, i64, i64, i64, vp]),
                 "ref_gqa_attention_paged": (C.c_int, [vp, u64, vp, i64, i64, i64, i64, vp]),
                 "ref_decode_batch": (None, [vp, i64, vp, i64, vp, i64, i64, i64, i64, vp]),
+                "ref_quantize_tensor": (None, [vp, i64, i64, vp, vp]),
+                "ref_matmul_quantized_blocked": (None, [vp, i64, i64, vp, vp, i64, vp]),
+                "ref_qt_new": (vp, [vp, vp, i64, i64]),
+                "ref_qt_free": (None, [vp]),
+                "ref_matmul_quantized": (None, [vp, i64, i64, vp, vp]),
             }
             for name, (res, args) in sig.items():
                 fn = getattr(lib, name)
@@ -131,6 +138,67 @@ def _load_ref():
 
 def _f32(a):
     return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _vp(a):
+    return a.ctypes.data_as(vp)
+
+
+# ---------------------------------------------------- int8 projections --
+
+def quantize_rows(w):
+    """quantize_tensor (src/quantized_tensor.cpp:9-47), restated:
+    (q int8 [rows, cols], scales fp32 [rows])."""
+    w = _f32(w)
+    rows, cols = w.shape
+    q = np.empty((rows, cols), np.int8)
+    sc = np.empty(rows, np.float32)
+    _load().kvo_quantize_rows(_vp(w), rows, cols, _vp(q), _vp(sc))
+    return q, sc
+
+
+def matmul_int8(x, q, scales):
+    """matmul_quantized_range_blocked (src/quantized_tensor.cpp:60-100),
+    restated: x [M, K] * (q [K, N] scaled per row) -> [M, N], k in order."""
+    x = _f32(x)
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    scales = _f32(scales)
+    M, K = x.shape
+    N = q.shape[1]
+    out = np.empty((M, N), np.float32)
+    _load().kvo_matmul_int8(_vp(x), M, K, _vp(q), _vp(scales), N, _vp(out))
+    return out
+
+
+def ref_quantize_rows(w):
+    """The reference's quantize_tensor itself (oracle/_ref)."""
+    w = _f32(w)
+    rows, cols = w.shape
+    q = np.empty((rows, cols), np.int8)
+    sc = np.empty(rows, np.float32)
+    _load_ref().ref_quantize_tensor(_vp(w), rows, cols, _vp(q), _vp(sc))
+    return q, sc
+
+
+def ref_matmul_int8(x, q, scales, threaded=False):
+    """The reference's matmul_quantized_range_blocked (one thread) or, with
+    `threaded`, matmul_quantized over its ThreadPool (oracle/_ref)."""
+    x = _f32(x)
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    scales = _f32(scales)
+    M, K = x.shape
+    N = q.shape[1]
+    out = np.empty((M, N), np.float32)
+    R = _load_ref()
+    if threaded:
+        qt = R.ref_qt_new(_vp(q), _vp(scales), K, N)
+        try:
+            R.ref_matmul_quantized(_vp(x), M, K, qt, _vp(out))
+        finally:
+            R.ref_qt_free(qt)
+    else:
+        R.ref_matmul_quantized_blocked(_vp(x), M, K, _vp(q), _vp(scales), N, _vp(out))
+    return out
 
 
 # ---------------------------------------------------------------- math ----

@@ -10,12 +10,15 @@
 //   rmsnorm (include/nn/rmsnorm.h:4)
 //   GQA_attention / GQA_attention_paged (include/nn/attention.h:8-10)
 //   ThreadPool::parallel_for (include/infer/thread_pool.h:14)
+//   quantize_tensor / matmul_quantized_range_blocked / matmul_quantized
+//     (include/core/quantized_tensor.h:14-23)
 #include <cstdint>
 #include <cstring>
 #include <memory>
 #include <stdexcept>
 #include <vector>
 
+#include "core/quantized_tensor.h"
 #include "infer/kv_block_pool.h"
 #include "infer/thread_pool.h"
 #include "nn/RoPE.h"
@@ -159,6 +162,42 @@ void ref_decode_batch(void** pools, int64_t n_layers, const uint64_t* seqs, int6
             copy_out(O, out + t * per);
         }
     });
+}
+
+// quantize_tensor on a [rows][cols] matrix: q (int8) and one scale per row.
+void ref_quantize_tensor(const float* w, int64_t rows, int64_t cols, int8_t* q, float* scales) {
+    Tensor t({(size_t)rows, (size_t)cols}, std::vector<scalar_t>(w, w + rows * cols));
+    QuantizedTensor qt = quantize_tensor(t);
+    std::memcpy(q, qt.data.data(), qt.data.size());
+    std::memcpy(scales, qt.scales.data(), qt.scales.size() * sizeof(float));
+}
+
+static QuantizedTensor make_qt(const int8_t* q, const float* s, int64_t K, int64_t N) {
+    QuantizedTensor qt;
+    qt.data.assign(q, q + K * N);
+    qt.scales.assign(s, s + K);
+    qt.rows = (size_t)K;
+    qt.cols = (size_t)N;
+    return qt;
+}
+
+// matmul_quantized_range_blocked over all columns, on the calling thread.
+void ref_matmul_quantized_blocked(const float* x, int64_t M, int64_t K, const int8_t* q, const float* s, int64_t N,
+                                  float* out) {
+    QuantizedTensor qt = make_qt(q, s, K, N);
+    matmul_quantized_range_blocked(x, qt, out, (size_t)M, (size_t)K, (size_t)N, 0, (size_t)N);
+}
+
+// matmul_quantized: the reference's public entry, fanned out over its
+// ThreadPool (get_pool()) when N >= 512.  `qt` is built once by
+// ref_qt_new so that a timed loop measures the multiply alone.
+void* ref_qt_new(const int8_t* q, const float* s, int64_t K, int64_t N) {
+    return new QuantizedTensor(make_qt(q, s, K, N));
+}
+void ref_qt_free(void* qt) { delete static_cast<QuantizedTensor*>(qt); }
+void ref_matmul_quantized(const float* x, int64_t M, int64_t K, void* qt, float* out) {
+    auto* w = static_cast<QuantizedTensor*>(qt);
+    copy_out(matmul_quantized(make_tensor(x, {(size_t)M, (size_t)K}), *w), out);
 }
 
 }  // extern "C"

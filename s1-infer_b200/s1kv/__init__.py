@@ -123,6 +123,8 @@ SIGNATURES = {
     "s1kv_batch_attention": (C.c_int, [vp, i32, vp, vp, i32, vp]),
     "s1kv_batch_layer_host": (C.c_int, [vp, i32, vp, vp, vp, vp, i32, vp]),
     "s1kv_batch_end": (C.c_int, [vp, vp]),
+    "s1kv_quantize_rows": (C.c_int, [vp, i64, i64, vp, vp, vp]),
+    "s1kv_matmul_int8": (C.c_int, [vp, i64, i64, vp, vp, i64, vp, vp]),
     "s1kv_launch_count": (i64, []),
     "s1kv_batch_plan": (C.c_int, [vp, P(i32), P(i64)]),
 }
@@ -532,6 +534,57 @@ def apply_rope(x, start_pos=0, theta=1.0e6, device=None):
         check(lib().s1kv_apply_rope(_dptr(x3), _dptr(out), start_pos, x3.shape[0], x3.shape[1], x3.shape[2], theta,
                                     _stream()))
     return out.reshape(shape)
+
+
+# ============================================== int8 projections ==========
+# quantize_tensor / dequantize / matmul_quantized (include/core/
+# quantized_tensor.h:7-23): the weights either side of the KV path, int8 with
+# one scale per row k of the pre-transposed [K, N] weight.
+
+class QuantizedTensor:
+    """struct QuantizedTensor (include/core/quantized_tensor.h:7-12): data
+    int8 [rows, cols] and scales fp32 [rows], both on the GPU."""
+
+    def __init__(self, data, scales):
+        self.data, self.scales = data, scales
+        self.rows, self.cols = int(data.shape[0]), int(data.shape[1])
+
+
+def quantize_tensor(t, device=None):
+    """quantize_tensor (src/quantized_tensor.cpp:9-47): a [rows, cols] float
+    tensor to int8 with scale max|row| / 127 per row (1 for a zero row) and
+    round(value / scale), ties away from zero; bit-exact."""
+    import torch
+    w = _cuda_f32(t, device)
+    if w.dim() != 2:
+        raise S1KVError(EINVAL, "quantize_tensor needs a 2-D tensor")
+    q = torch.empty(w.shape, dtype=torch.int8, device=w.device)
+    sc = torch.empty((w.shape[0],), dtype=torch.float32, device=w.device)
+    with torch.cuda.device(w.device):
+        check(lib().s1kv_quantize_rows(_dptr(w), w.shape[0], w.shape[1], _dptr(q), _dptr(sc), _stream()))
+    return QuantizedTensor(q, sc)
+
+
+def dequantize(qt, row, col):
+    """dequantize (src/quantized_tensor.cpp:49-57): q[row, col] * scale[row]."""
+    import numpy as np
+    return float(np.float32(int(qt.data[row, col])) * np.float32(float(qt.scales[row])))
+
+
+def matmul_quantized(x, w, out=None):
+    """matmul_quantized (src/quantized_tensor.cpp:102-122): x [M, K] float
+    times the quantized [K, N] weight -> [M, N] fp32 (within 2e-5 of the
+    output scale of the reference's sequential sum)."""
+    import torch
+    xd = _cuda_f32(x, w.data.device.index)
+    if xd.dim() != 2 or xd.shape[1] != w.rows:
+        raise S1KVError(EINVAL, "matmul_quantized: x must be [M, %d]" % w.rows)
+    if out is None:
+        out = torch.empty((xd.shape[0], w.cols), dtype=torch.float32, device=xd.device)
+    with torch.cuda.device(xd.device):
+        check(lib().s1kv_matmul_int8(_dptr(xd), xd.shape[0], w.rows, _dptr(w.data), _dptr(w.scales), w.cols,
+                                     _dptr(out), _stream()))
+    return out
 
 
 # ================================================ KV-head-sharded serving ==

@@ -8,6 +8,9 @@ Writes:
   rope.npz        apply_rope outputs (src/nn/RoPE.cpp) for seeded inputs
   pool_ops.npz    KVBlockPool bookkeeping (status, length, block table)
                   after every op of seeded op scripts
+  int8.npz        quantize_tensor / matmul_quantized outputs
+                  (src/quantized_tensor.cpp) on the inputs of the reference's
+                  tests/test_quantized_tensor.cpp and on seeded matrices
   <scenario>.npz  paged-attention outputs and block tables of the scenarios
                   in scenarios.py (prefill + decode through KVBlockPool,
                   apply_rope, GQA_attention_paged)
@@ -98,12 +101,49 @@ def make_pool_ops():
     np.savez_compressed(os.path.join(HERE, "pool_ops.npz"), **out)
 
 
+def int8_cases():
+    """(name, w [K, N], x [M, K]) inputs of the int8 fixtures."""
+    cases = []
+    # tests/test_quantized_tensor.cpp:5-23, 26-39, 42-49
+    cases.append(("kat_2x3", np.array([[1.0, -2.0, 0.5], [10.0, -20.0, 5.0]], np.float32),
+                  np.array([[0.5, -1.0]], np.float32)))
+    cases.append(("kat_per_row", np.array([[0.01, 0.02], [1.0, 2.0]], np.float32), np.array([[1.0, 1.0]], np.float32)))
+    cases.append(("kat_zero_row", np.zeros((1, 2), np.float32), np.array([[3.0]], np.float32)))
+    # tests/test_quantized_tensor.cpp:51-75: M 2, K 80, N 88.  The index
+    # expressions are size_t: (i * 13) % 200 - 100 wraps below zero to about
+    # 2^64, which becomes 1.8446744e19f before the 0.01f scale.
+    def ref_fill(n, mul):
+        i = np.arange(n, dtype=np.uint64)
+        v = ((i * np.uint64(mul)) % np.uint64(200)) - np.uint64(100)  # wraps like size_t
+        return (np.float32(0.01) * v.astype(np.float32)).astype(np.float32)
+    cases.append(("kat_blocked", ref_fill(80 * 88, 7).reshape(80, 88), ref_fill(2 * 80, 13).reshape(2, 80)))
+    rng = np.random.default_rng(11)
+    for name, (M, K, N) in {"rand_1x384x136": (1, 384, 136), "rand_3x257x131": (3, 257, 131),
+                            "rand_9x200x72": (9, 200, 72)}.items():
+        w = (rng.standard_normal((K, N)) * rng.uniform(0.01, 2.0, size=(K, 1))).astype(np.float32)
+        w[5] = 0.0  # an all-zero row
+        cases.append((name, w, rng.standard_normal((M, K)).astype(np.float32)))
+    return cases
+
+
+def make_int8():
+    out = {}
+    for name, w, x in int8_cases():
+        q, sc = O.ref_quantize_rows(w)
+        out[f"{name}/w"], out[f"{name}/x"] = w, x
+        out[f"{name}/q"], out[f"{name}/scales"] = q, sc
+        out[f"{name}/out"] = O.ref_matmul_int8(x, q, sc)
+        assert np.array_equal(out[f"{name}/out"].view(np.uint32), O.ref_matmul_int8(x, q, sc, threaded=True).view(np.uint32))
+    np.savez_compressed(os.path.join(HERE, "int8.npz"), **out)
+
+
 def main():
     O.build()
     if not O.ref_available():
         sys.exit("oracle/_ref/libs1ref.so missing: the reference sources are needed to make fixtures")
     make_rope()
     make_pool_ops()
+    make_int8()
     for name in S.SCENARIOS:
         res = S.run_scenario(name, RefBackend())
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **S.flatten(res, name))
