@@ -1,7 +1,8 @@
 // test_shim.cpp -- the C++ reference-interface shim (KVBlockPool, KVView,
-// GQA_attention(_paged), apply_rope) on the GPU, against the known answers
-// of the reference's own tests: tests/test_kv_block_pool.cpp:6-207,
-// tests/test_attention.cpp:5-120, tests/test_rope.cpp:5-34.
+// GQA_attention(_paged), apply_rope, quantize_tensor / matmul_quantized) on
+// the GPU, against the known answers of the reference's own tests:
+// tests/test_kv_block_pool.cpp:6-207, tests/test_attention.cpp:5-120,
+// tests/test_rope.cpp:5-34, tests/test_quantized_tensor.cpp:5-75.
 // Exit status 0 when every check passes.
 #include <cmath>
 #include <cstdio>
@@ -10,6 +11,7 @@
 #include <stdexcept>
 #include <vector>
 
+#include "core/quantized_tensor.h"
 #include "infer/kv_block_pool.h"
 #include "nn/RoPE.h"
 #include "nn/attention.h"
@@ -171,10 +173,64 @@ static void rope_cases() {
     EXPECT(std::fabs(y1->at({0, 1})) < 1e-3f && std::fabs(y1->at({0, 3})) < 1e-3f);
 }
 
+static void quantized_cases() {
+    // tests/test_quantized_tensor.cpp:5-23: recovered within 2% of each value
+    {
+        Tensor t(std::vector<size_t>{2, 3}, std::vector<float>{1.0f, -2.0f, 0.5f, 10.0f, -20.0f, 5.0f});
+        QuantizedTensor qt = quantize_tensor(t);
+        EXPECT(qt.rows == 2 && qt.cols == 3);
+        for (size_t r = 0; r < 2; r++)
+            for (size_t c = 0; c < 3; c++) EXPECT(near(dequantize(qt, r, c), t.at({r, c}), 0.02f));
+    }
+    // :25-39: each row its own scale
+    {
+        auto t = std::make_shared<Tensor>(std::vector<size_t>{2, 2}, std::vector<float>{0.01f, 0.02f, 1.0f, 2.0f});
+        QuantizedTensor qt = quantize_tensor(*t);
+        EXPECT(!near(qt.scales[0], qt.scales[1], 1e-3f));
+        EXPECT(near(dequantize(qt, 0, 0), 0.01f, 0.02f) && near(dequantize(qt, 0, 1), 0.02f, 0.02f));
+    }
+    // :41-49: an all-zero row gives zeros, not NaN
+    {
+        auto t = std::make_shared<Tensor>(std::vector<size_t>{1, 2}, std::vector<float>{0.0f, 0.0f});
+        QuantizedTensor qt = quantize_tensor(*t);
+        EXPECT(dequantize(qt, 0, 0) == 0.0f && dequantize(qt, 0, 1) == 0.0f);
+    }
+    // :51-75: blocked product close to the float product (5% of max), with a
+    // tail that is not a multiple of 8 (index expressions signed here, so all
+    // values stay O(1)); here on a column range as well
+    {
+        const size_t M = 2, K = 80, N = 88;
+        std::vector<float> a(M * K), b(K * N);
+        for (size_t i = 0; i < M * K; i++) a[i] = 0.01f * (float)((int)((i * 13) % 200) - 100);
+        for (size_t i = 0; i < K * N; i++) b[i] = 0.01f * (float)((int)((i * 7) % 200) - 100);
+        auto bt = std::make_shared<Tensor>(std::vector<size_t>{K, N}, b);
+        QuantizedTensor qb = quantize_tensor(*bt);
+        std::vector<double> ref(M * N, 0.0);
+        double mx = 0;
+        for (size_t i = 0; i < M; i++)
+            for (size_t j = 0; j < N; j++) {
+                for (size_t k = 0; k < K; k++) ref[i * N + j] += (double)a[i * K + k] * b[k * N + j];
+                mx = std::fmax(mx, std::fabs(ref[i * N + j]));
+            }
+        std::vector<float> out(M * N, -1.0f);
+        matmul_quantized_range_blocked(a.data(), qb, out.data(), M, K, N, 0, N);
+        for (size_t i = 0; i < M * N; i++) EXPECT(std::fabs(out[i] - ref[i]) < 0.05 * mx);
+        std::vector<float> part(M * N, -7.0f);
+        matmul_quantized_range_blocked(a.data(), qb, part.data(), M, K, N, 40, 88);
+        for (size_t i = 0; i < M; i++)
+            for (size_t j = 0; j < N; j++) EXPECT(j < 40 ? part[i * N + j] == -7.0f : part[i * N + j] == out[i * N + j]);
+        auto x = std::make_shared<Tensor>(std::vector<size_t>{M, K}, a);
+        auto y = matmul_quantized(x, qb);
+        EXPECT(y->shape() == (std::vector<size_t>{M, N}));
+        for (size_t i = 0; i < M * N; i++) EXPECT(y->data()[i] == out[i]);
+    }
+}
+
 int main() {
     pool_cases();
     attention_cases();
     rope_cases();
+    quantized_cases();
     std::printf("%d checks, %d failed\n", g_checks, g_failed);
     return g_failed ? 1 : 0;
 }

@@ -28,6 +28,10 @@ EXPECTED = [
     "GQA_attention(std::shared_ptr<Tensor> const&, std::shared_ptr<Tensor> const&, std::shared_ptr<Tensor> const&, unsigned long, unsigned long, unsigned long)",
     "apply_rope(std::shared_ptr<Tensor> const&, unsigned long)",
     "reshape_to_heads(std::shared_ptr<Tensor> const&, unsigned long, unsigned long)",
+    "quantize_tensor(Tensor const&)",
+    "dequantize(QuantizedTensor const&, unsigned long, unsigned long)",
+    "matmul_quantized(std::shared_ptr<Tensor> const&, QuantizedTensor const&)",
+    "matmul_quantized_range_blocked(float const*, QuantizedTensor const&, float*, unsigned long, unsigned long, unsigned long, unsigned long, unsigned long)",
 ]
 
 
