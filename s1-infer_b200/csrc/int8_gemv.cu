@@ -110,6 +110,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) matmul_int8_kernel(const floa
     const int k0 = blockIdx.y * rows_per_cta;
     const int k_end = min(K, k0 + rows_per_cta);
     const int rows_per_warp = rows_per_cta / kGemvWarps;
+    // a split over K reduces through the cluster's shared memory: announce
+    // that this CTA has started (waited for before the first remote store)
+    if (gridDim.y > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
     const int c = n0 + CPL * lane;  // this lane's columns [c, c + CPL)
     const int wr0 = warp * rows_per_warp;
@@ -193,38 +196,42 @@ __global__ void __launch_bounds__(kGemvThreads, 1) matmul_int8_kernel(const floa
         for (int j = 0; j < CPL / 2; j++)
             *reinterpret_cast<float2*>(&red[(warp * MB + m) * NC + CPL * lane + 2 * j]) = acc[m][j];
     __syncthreads();
+    if (gridDim.y == 1) {
+        for (int i = tid; i < MB * NC; i += kGemvThreads) {
+            float s = red[i];
+#pragma unroll
+            for (int wi = 1; wi < kGemvWarps; wi++) s += red[wi * MB * NC + i];
+            const int m = i / NC, cc = i % NC;
+            if (m0 + m < M && n0 + cc < N) out[(size_t)(m0 + m) * N + n0 + cc] = s;
+        }
+        return;
+    }
+    // K split over the cluster.  Rank o owns columns [o * per, (o + 1) * per);
+    // every rank stores its partial of those columns into slot `rank` of the
+    // owner's buffer (distributed shared memory: remote stores pipeline, remote
+    // loads would not), one release/acquire cluster barrier makes them
+    // visible, and each owner sums its slots in rank order.  Every peer has
+    // started (the arrive at entry) before the first remote store, and after
+    // the barrier no CTA touches another's memory, so CTAs exit freely.
+    cg::cluster_group cluster = cg::this_cluster();
+    const int cs = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
+    const int per = NC / cs;
+    float* recv = part;  // [cs][MB][per]
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // peers started
     for (int i = tid; i < MB * NC; i += kGemvThreads) {
         float s = red[i];
 #pragma unroll
         for (int wi = 1; wi < kGemvWarps; wi++) s += red[wi * MB * NC + i];
-        part[i] = s;
+        const int m = i / NC, cc = i % NC, owner = cc / per;
+        cluster.map_shared_rank(recv, owner)[(rank * MB + m) * per + cc % per] = s;
     }
-    if (gridDim.y == 1) {
-        __syncthreads();
-        for (int i = tid; i < MB * NC; i += kGemvThreads) {
-            const int m = i / NC, cc = i % NC;
-            if (m0 + m < M && n0 + cc < N) out[(size_t)(m0 + m) * N + n0 + cc] = part[i];
-        }
-        return;
-    }
-    // K split over the cluster: rank r sums every rank's partial for columns
-    // [r * NC / cs, (r + 1) * NC / cs), in rank order.
-    cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
-    const int cs = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
-    const int per = NC / cs;
     for (int i = tid; i < MB * per; i += kGemvThreads) {
-        const int m = i / per, cc = rank * per + i % per;
-        float v[kMaxCluster];
-#pragma unroll
-        for (int rr = 0; rr < kMaxCluster; rr++)  // all remote loads in flight together
-            v[rr] = rr < cs ? cluster.map_shared_rank(part, rr)[m * NC + cc] : 0.0f;
-        float s = v[0];
-#pragma unroll
-        for (int rr = 1; rr < kMaxCluster; rr++) s += v[rr];  // rank order (the zeros past cs are exact)
+        const int m = i / per, cl = i % per, cc = rank * per + cl;
+        float s = recv[m * per + cl];
+        for (int rr = 1; rr < cs; rr++) s += recv[(rr * MB + m) * per + cl];
         if (m0 + m < M && n0 + cc < N) out[(size_t)(m0 + m) * N + n0 + cc] = s;
     }
-    cluster.sync();  // no CTA leaves while another reads its partial
 }
 
 // One warp per row: scale = max|row| / 127 (1 for an all-zero row), then
