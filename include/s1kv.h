@@ -388,6 +388,13 @@ int s1kv_quantize_rows(const float* w, int64_t rows, int64_t cols, int8_t* q, fl
  * M any (rows of x are taken 8 at a time). */
 int s1kv_matmul_int8(const float* x, int64_t M, int64_t K, const int8_t* q, const float* scales, int64_t N,
                      float* out, void* stream);
+/* Up to 4 products sharing x and K in one launch (the q/k/v projections of
+ * self_attention_quantized, src/nn/attention.cpp:307-309; gate/up of the
+ * MLP, src/nn/mlp.cpp:81-82): out[i] [M][N[i]] = x * (q[i], scales[i]).
+ * The same results as n_mats separate s1kv_matmul_int8 calls; the arrays
+ * (host memory) hold device pointers. */
+int s1kv_matmul_int8_group(const float* x, int64_t M, int64_t K, int32_t n_mats, const int8_t* const* q,
+                           const float* const* scales, const int64_t* N, float* const* out, void* stream);
 
 /* ======================== introspection ======================== */
 

@@ -36,6 +36,8 @@
 //     Quantization is bit-exact (IEEE division, round half away from zero).
 #include <cooperative_groups.h>
 
+#include <algorithm>
+
 #include "internal.h"
 
 namespace cg = cooperative_groups;
@@ -93,19 +95,40 @@ __device__ __forceinline__ void load_bytes(const int8_t* row, int c, int N, uint
     }
 }
 
+// Up to kMaxGroup products sharing x and K (q/k/v; gate/up) in one launch:
+// the grid's x dimension runs over every matrix's column tiles, matrix i
+// starting at tile `tile0`.
+constexpr int kMaxGroup = 4;
+struct GemvMat {
+    const int8_t* q;
+    const float* scales;
+    float* out;
+    int N, tile0, vec_loads;
+};
+struct GemvGroup {
+    GemvMat m[kMaxGroup];
+    int n;
+};
+
 template <int MB, int CPL>
 __global__ void __launch_bounds__(kGemvThreads, 1) matmul_int8_kernel(const float* __restrict__ x, int M, int K,
-                                                                    const int8_t* __restrict__ q,
-                                                                    const float* __restrict__ scales, int N,
-                                                                    float* __restrict__ out, int rows_per_cta,
-                                                                    int vec_loads) {
+                                                                    const __grid_constant__ GemvGroup grp,
+                                                                    int rows_per_cta) {
     constexpr int NC = GemvTile<MB, CPL>::NC, kChunk = GemvTile<MB, CPL>::CHUNK;
     extern __shared__ float gemv_smem[];
     float* xs = gemv_smem;                   // [MB][rows_per_cta]: x * scale
     float* red = xs + MB * rows_per_cta;     // [warps][MB][NC]
     float* part = red + kGemvWarps * MB * NC;  // [MB][NC]: this CTA's partial
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * NC;
+    int mi = 0;  // this CTA's matrix (uniform)
+#pragma unroll
+    for (int i = 1; i < kMaxGroup; i++)
+        if (i < grp.n && (int)blockIdx.x >= grp.m[i].tile0) mi = i;
+    const int8_t* __restrict__ q = grp.m[mi].q;
+    const float* __restrict__ scales = grp.m[mi].scales;
+    float* __restrict__ out = grp.m[mi].out;
+    const int N = grp.m[mi].N, vec_loads = grp.m[mi].vec_loads;
+    const int n0 = ((int)blockIdx.x - grp.m[mi].tile0) * NC;
     const int m0 = blockIdx.z * MB;
     const int k0 = blockIdx.y * rows_per_cta;
     const int k_end = min(K, k0 + rows_per_cta);
@@ -258,8 +281,7 @@ struct GemvShape {
 };
 
 template <int MB, int CPL>
-int launch_gemv(const float* x, int M, int K, const int8_t* q, const float* scales, int N, float* out,
-                const GemvShape& g, cudaStream_t stream) {
+int launch_gemv(const float* x, int M, int K, GemvGroup grp, const GemvShape& g, cudaStream_t stream) {
     auto kern = matmul_int8_kernel<MB, CPL>;
     static bool attrs_set = false;
     if (!attrs_set) {
@@ -267,9 +289,15 @@ int launch_gemv(const float* x, int M, int K, const int8_t* q, const float* scal
         S1KV_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemMax));
         attrs_set = true;
     }
-    const int vec_loads = (N % CPL == 0) && ((reinterpret_cast<uintptr_t>(q) % CPL) == 0);
+    int tiles = 0;
+    for (int i = 0; i < grp.n; i++) {
+        GemvMat& m = grp.m[i];
+        m.vec_loads = (m.N % CPL == 0) && ((reinterpret_cast<uintptr_t>(m.q) % CPL) == 0);
+        m.tile0 = tiles;
+        tiles += (m.N + 32 * CPL - 1) / (32 * CPL);
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)g.col_tiles, (unsigned)g.cs, (unsigned)g.z);
+    cfg.gridDim = dim3((unsigned)tiles, (unsigned)g.cs, (unsigned)g.z);
     cfg.blockDim = dim3(kGemvThreads);
     cfg.dynamicSmemBytes = g.smem;
     cfg.stream = stream;
@@ -285,7 +313,7 @@ int launch_gemv(const float* x, int M, int K, const int8_t* q, const float* scal
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    S1KV_CUDA(cudaLaunchKernelEx(&cfg, kern, x, M, K, q, scales, N, out, g.rows_per_cta, vec_loads));
+    S1KV_CUDA(cudaLaunchKernelEx(&cfg, kern, x, M, K, grp, g.rows_per_cta));
     g_launches++;
     return S1KV_OK;
 }
@@ -367,30 +395,58 @@ extern "C" int s1kv_quantize_rows(const float* w, int64_t rows, int64_t cols, in
     return S1KV_OK;
 }
 
-extern "C" int s1kv_matmul_int8(const float* x, int64_t M, int64_t K, const int8_t* q, const float* scales, int64_t N,
-                                float* out, void* stream) {
-    if (M < 0 || K < 0 || N < 0 || M > (1 << 30) || K > (1 << 30) || N > (1 << 30))
-        return set_error(S1KV_EINVAL, "matmul_int8: bad shape");
-    if (M == 0 || N == 0) return S1KV_OK;
-    if (!x || !q || !scales || !out) return set_error(S1KV_EINVAL, "matmul_int8: null pointer");
+static int matmul_int8_group(const float* x, int64_t M, int64_t K, int32_t n, const int8_t* const* q,
+                             const float* const* scales, const int64_t* N, float* const* out, cudaStream_t s) {
+    if (n < 1 || n > kMaxGroup) return set_error(S1KV_EINVAL, "matmul_int8: 1 to %d matrices per launch", kMaxGroup);
+    if (M < 0 || K < 0 || M > (1 << 30) || K > (1 << 30)) return set_error(S1KV_EINVAL, "matmul_int8: bad shape");
+    GemvGroup grp = {};
+    int64_t total_n = 0;
+    for (int i = 0; i < n; i++) {
+        if (N[i] < 0 || N[i] > (1 << 30)) return set_error(S1KV_EINVAL, "matmul_int8: bad shape");
+        if (M > 0 && N[i] > 0 && (!x || !q[i] || !scales[i] || !out[i]))
+            return set_error(S1KV_EINVAL, "matmul_int8: null pointer");
+        if (N[i] == 0) continue;  // nothing to compute for this one
+        grp.m[grp.n].q = q[i];
+        grp.m[grp.n].scales = scales[i];
+        grp.m[grp.n].out = out[i];
+        grp.m[grp.n].N = (int)N[i];
+        grp.n++;
+        total_n += N[i];
+    }
+    if (M == 0 || grp.n == 0) return S1KV_OK;
     if (K == 0) {
-        S1KV_CUDA(cudaMemsetAsync(out, 0, sizeof(float) * (size_t)M * (size_t)N, (cudaStream_t)stream));
+        for (int i = 0; i < grp.n; i++)
+            S1KV_CUDA(cudaMemsetAsync(grp.m[i].out, 0, sizeof(float) * (size_t)M * (size_t)grp.m[i].N, s));
         return S1KV_OK;
     }
     int dev = 0, sms = 148;
     S1KV_CUDA(cudaGetDevice(&dev));
     S1KV_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     GemvShape g;
-    int st = gemv_shape((int)M, (int)K, (int)N, sms, gemv_cluster_cap(dev), &g);
+    // the shape follows the group's widest matrix (narrow or wide loads)
+    int widest = 0;
+    for (int i = 0; i < grp.n; i++) widest = std::max(widest, grp.m[i].N);
+    int st = gemv_shape((int)M, (int)K, widest, sms, gemv_cluster_cap(dev), &g);
     if (st) return st;
-    const cudaStream_t s = (cudaStream_t)stream;
-    const int Mi = (int)M, Ki = (int)K, Ni = (int)N;
+    (void)total_n;
+    const int Mi = (int)M, Ki = (int)K;
 #define S1KV_GEMV(MB_, CPL_) \
-    if (g.mb == MB_ && g.cpl == CPL_) return launch_gemv<MB_, CPL_>(x, Mi, Ki, q, scales, Ni, out, g, s);
+    if (g.mb == MB_ && g.cpl == CPL_) return launch_gemv<MB_, CPL_>(x, Mi, Ki, grp, g, s);
     S1KV_GEMV(1, 4) S1KV_GEMV(1, 8) S1KV_GEMV(1, 16)
     S1KV_GEMV(2, 4) S1KV_GEMV(2, 8) S1KV_GEMV(2, 16)
     S1KV_GEMV(4, 4) S1KV_GEMV(4, 8)
     S1KV_GEMV(8, 4)
 #undef S1KV_GEMV
     return set_error(S1KV_EINVAL, "matmul_int8: no kernel for %d rows x %d columns per lane", g.mb, g.cpl);
+}
+
+extern "C" int s1kv_matmul_int8(const float* x, int64_t M, int64_t K, const int8_t* q, const float* scales, int64_t N,
+                                float* out, void* stream) {
+    return matmul_int8_group(x, M, K, 1, &q, &scales, &N, &out, (cudaStream_t)stream);
+}
+
+extern "C" int s1kv_matmul_int8_group(const float* x, int64_t M, int64_t K, int32_t n_mats, const int8_t* const* q,
+                                      const float* const* scales, const int64_t* N, float* const* out, void* stream) {
+    if (!q || !scales || !N || !out) return set_error(S1KV_EINVAL, "matmul_int8_group: null array");
+    return matmul_int8_group(x, M, K, n_mats, q, scales, N, out, (cudaStream_t)stream);
 }

@@ -125,6 +125,7 @@ SIGNATURES = {
     "s1kv_batch_end": (C.c_int, [vp, vp]),
     "s1kv_quantize_rows": (C.c_int, [vp, i64, i64, vp, vp, vp]),
     "s1kv_matmul_int8": (C.c_int, [vp, i64, i64, vp, vp, i64, vp, vp]),
+    "s1kv_matmul_int8_group": (C.c_int, [vp, i64, i64, i32, vp, vp, vp, vp, vp]),
     "s1kv_launch_count": (i64, []),
     "s1kv_batch_plan": (C.c_int, [vp, P(i32), P(i64)]),
 }
@@ -585,6 +586,26 @@ def matmul_quantized(x, w, out=None):
         check(lib().s1kv_matmul_int8(_dptr(xd), xd.shape[0], w.rows, _dptr(w.data), _dptr(w.scales), w.cols,
                                      _dptr(out), _stream()))
     return out
+
+
+def matmul_quantized_group(x, ws, outs=None):
+    """Products of one x with up to 4 quantized weights of the same K in one
+    launch (q/k/v, gate/up): the same results as matmul_quantized on each."""
+    import torch
+    dev = ws[0].data.device.index
+    xd = _cuda_f32(x, dev)
+    if xd.dim() != 2 or any(w.rows != xd.shape[1] for w in ws):
+        raise S1KVError(EINVAL, "matmul_quantized_group: x must be [M, K] with K the weights' rows")
+    if outs is None:
+        outs = [torch.empty((xd.shape[0], w.cols), dtype=torch.float32, device=xd.device) for w in ws]
+    n = len(ws)
+    qa = (vp * n)(*[w.data.data_ptr() for w in ws])
+    sa = (vp * n)(*[w.scales.data_ptr() for w in ws])
+    na = (i64 * n)(*[w.cols for w in ws])
+    oa = (vp * n)(*[o.data_ptr() for o in outs])
+    with torch.cuda.device(xd.device):
+        check(lib().s1kv_matmul_int8_group(_dptr(xd), xd.shape[0], xd.shape[1], n, qa, sa, na, oa, _stream()))
+    return outs
 
 
 # ================================================ KV-head-sharded serving ==

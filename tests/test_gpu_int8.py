@@ -129,3 +129,31 @@ def test_matmul_empty(s1kv, cuda):
                               torch.ones(16, dtype=torch.float32, device="cuda"))
     out = s1kv.matmul_quantized(torch.zeros((2, 16), device="cuda"), qt)
     assert tuple(out.shape) == (2, 0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_group_equals_separate(s1kv, oracle, cuda, M):
+    # q/k/v of self_attention_quantized (src/nn/attention.cpp:307-309) in one launch
+    torch = cuda
+    rng = np.random.default_rng(90 + M)
+    K = 1024
+    ws = [(rng.standard_normal((K, N)) * 0.05).astype(np.float32) for N in (2048, 1024, 1024)]
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    qts = [s1kv.quantize_tensor(w) for w in ws]
+    grouped = [o.cpu().numpy() for o in s1kv.matmul_quantized_group(x, qts)]
+    for qt, g in zip(qts, grouped):
+        sep = s1kv.matmul_quantized(x, qt).cpu().numpy()
+        assert np.array_equal(bits(g), bits(sep))
+        ref = oracle.matmul_int8(x, qt.data.cpu().numpy(), qt.scales.cpu().numpy())
+        ok, rel = close(g, ref)
+        assert ok, rel
+
+
+@pytest.mark.gpu
+def test_group_limits(s1kv, cuda):
+    torch = cuda
+    qt = s1kv.quantize_tensor(np.ones((16, 8), np.float32))
+    with pytest.raises(s1kv.S1KVError) as e:
+        s1kv.matmul_quantized_group(np.ones((1, 16), np.float32), [qt] * 5)
+    assert e.value.status == s1kv.EINVAL
