@@ -824,7 +824,8 @@ def run_ours(args):
         elif rank == 0:
             r = res[args.only]
             print(json.dumps({"profiling_case": args.only, "layers": LAYERS, "ms_per_step": r["elapsed_ms"] / args.steps,
-                              "avg_launch_ms": r["avg_launch_ms"], "bytes_per_launch": r["bytes_per_launch"]}))
+                              "avg_launch_ms": r["avg_launch_ms"], "bytes_per_launch": r["bytes_per_launch"],
+                              "e2e_ms_per_step": r["e2e_ms"] / args.steps if "e2e_ms" in r else None}))
         if world > 1:
             import torch.distributed as dist
             dist.barrier()

@@ -360,8 +360,13 @@ int s1kv_batch_append(s1kv_batch* batch, int32_t layer, const float* k, const fl
 int s1kv_batch_attention(s1kv_batch* batch, int32_t layer, const float* q, float* out, int32_t n_q_heads,
                          void* stream);
 /* End-to-end layer step with HOST buffers (pinned for full speed): copies
- * q, k, v in, runs RoPE+append and attention, copies out back.  Shapes as
- * above.  The copies are stream-ordered; synchronise before reading out. */
+ * q, k, v in, runs RoPE+append and attention on `stream`, copies out back.
+ * Shapes as above.  The copies run on the pool's own copy streams, two
+ * buffer slots alternating between calls, so one call's inputs go up while
+ * the previous call's kernels run and its output comes back during the
+ * next call's.  h_q/h_k/h_v may be reused once the stream has passed the
+ * call; h_out of every call of the batch is complete once the stream has
+ * passed s1kv_batch_end (synchronise then). */
 int s1kv_batch_layer_host(s1kv_batch* batch, int32_t layer, const float* h_q, const float* h_k, const float* h_v,
                           float* h_out, int32_t n_q_heads, void* stream);
 int s1kv_batch_end(s1kv_batch* batch, void* stream);

@@ -494,15 +494,24 @@ int s1kv_batch_layer_host(s1kv_batch* b, int32_t layer, const float* h_q, const 
     const int64_t D = p->desc.head_dim, Hkv = p->desc.num_kv_heads;
     const size_t qb = (size_t)b->n_rows * Hq * D * 4, kb = (size_t)b->n_tokens * Hkv * D * 4;
     const size_t oq = 0, ok = align16(qb), ov = ok + align16(kb), oqr = ov + align16(kb), oo = oqr + align16(qb),
-                 total = oo + align16(qb);
-    int st = p->io.ensure(total);
+                 slot_bytes = align16(oo + align16(qb));
+    int st = p->io.ensure(2 * slot_bytes);
     if (st) return st;
-    char* d = (char*)p->io.p;
-    if (qb) S1KV_CUDA(cudaMemcpyAsync(d + oq, h_q, qb, cudaMemcpyHostToDevice, stream));
+    // Two slots alternate between calls: the inputs of this call go up on
+    // the copy stream while the previous call's kernels run, and its output
+    // comes back on the second copy stream while the next call's run.
+    const int s = b->io_calls++ & 1;
+    char* d = (char*)p->io.p + s * slot_bytes;
+    cudaEvent_t in_ready = p->io_ev[s], slot_done = p->io_ev[2 + s], out_done = p->io_ev[4 + s];
+    if (p->io_slot_used[s]) S1KV_CUDA(cudaStreamWaitEvent(p->copy_stream, slot_done, 0));  // inputs consumed
+    if (qb) S1KV_CUDA(cudaMemcpyAsync(d + oq, h_q, qb, cudaMemcpyHostToDevice, p->copy_stream));
     if (kb) {
-        S1KV_CUDA(cudaMemcpyAsync(d + ok, h_k, kb, cudaMemcpyHostToDevice, stream));
-        S1KV_CUDA(cudaMemcpyAsync(d + ov, h_v, kb, cudaMemcpyHostToDevice, stream));
+        S1KV_CUDA(cudaMemcpyAsync(d + ok, h_k, kb, cudaMemcpyHostToDevice, p->copy_stream));
+        S1KV_CUDA(cudaMemcpyAsync(d + ov, h_v, kb, cudaMemcpyHostToDevice, p->copy_stream));
     }
+    S1KV_CUDA(cudaEventRecord(in_ready, p->copy_stream));
+    S1KV_CUDA(cudaStreamWaitEvent(stream, in_ready, 0));
+    if (p->io_slot_used[s]) S1KV_CUDA(cudaStreamWaitEvent(stream, out_done, 0));  // the slot's output read back
     const bool q_rows_are_tokens = b->n_rows == b->n_tokens && b->n_tokens > 0;
     st = s1kv_batch_rope_append(b, layer, q_rows_are_tokens ? (const float*)(d + oq) : nullptr, (float*)(d + oqr), Hq,
                                 (const float*)(d + ok), (const float*)(d + ov), stream);
@@ -510,7 +519,11 @@ int s1kv_batch_layer_host(s1kv_batch* b, int32_t layer, const float* h_q, const 
     const float* qa = q_rows_are_tokens ? (const float*)(d + oqr) : (const float*)(d + oq);
     st = s1kv_batch_attention(b, layer, qa, (float*)(d + oo), Hq, stream);
     if (st) return st;
-    if (qb) S1KV_CUDA(cudaMemcpyAsync(h_out, d + oo, qb, cudaMemcpyDeviceToHost, stream));
+    S1KV_CUDA(cudaEventRecord(slot_done, stream));
+    S1KV_CUDA(cudaStreamWaitEvent(p->d2h_stream, slot_done, 0));
+    if (qb) S1KV_CUDA(cudaMemcpyAsync(h_out, d + oo, qb, cudaMemcpyDeviceToHost, p->d2h_stream));
+    S1KV_CUDA(cudaEventRecord(out_done, p->d2h_stream));
+    p->io_slot_used[s] = true;
     return S1KV_OK;
 }
 
@@ -518,6 +531,11 @@ int s1kv_batch_end(s1kv_batch* b, void* stream) {
     if (!b) return S1KV_OK;
     S1KV_ON_DEVICE(b->pool->device);
     int st = S1KV_OK;
+    // host outputs of s1kv_batch_layer_host are complete once the stream
+    // passes this point
+    for (int s = 0; s < 2 && s < b->io_calls; s++)
+        if (cudaStreamWaitEvent((cudaStream_t)stream, b->pool->io_ev[4 + s], 0) != cudaSuccess)
+            st = set_error(S1KV_ECUDA, "s1kv_batch_end: waiting for host copies");
     if (b->seg) st = b->pool->stager.release(b->seg, (cudaStream_t)stream);
     delete b;
     return st;

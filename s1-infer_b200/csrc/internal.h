@@ -252,9 +252,15 @@ struct s1kv_pool {
     s1kv::DevBuf scratch;             // split-K partials
     s1kv::DevBuf counters;            // split-K arrival counters (kept at zero)
     s1kv::DevBuf late_meta;           // rows + work list planned after batch_begin
-    s1kv::DevBuf io;                  // host-pointer step buffers
+    s1kv::DevBuf io;                  // host-pointer step buffers: two slots
+    // s1kv_batch_layer_host: inputs go up on copy_stream and outputs come back
+    // on d2h_stream, overlapped with the kernels of neighbouring calls.
+    // io_ev: [0,1] inputs of slot s landed, [2,3] slot s's kernels done,
+    // [4,5] slot s's output copied back.
     cudaStream_t copy_stream = nullptr;
-    cudaEvent_t io_ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    cudaStream_t d2h_stream = nullptr;
+    cudaEvent_t io_ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    bool io_slot_used[2] = {false, false};
 };
 
 // Peer exchange of attention outputs for KV-head sharding (exchange.cu).
@@ -291,6 +297,7 @@ struct s1kv_batch {
     std::vector<s1kv::WorkItem> items;  // split-K work list (host copy)
     bool items_planned = false;       // rows' split fields and items computed
     bool items_uploaded = false;      // d_rows / d_items carry them
+    int32_t io_calls = 0;             // s1kv_batch_layer_host calls (slot = calls & 1)
 };
 
 namespace s1kv {

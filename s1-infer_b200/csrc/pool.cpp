@@ -435,7 +435,8 @@ int s1kv_pool_create(const s1kv_pool_desc* d, int device, s1kv_pool** out) {
         if (e == cudaSuccess)
             e = cudaMemset(p->d_table, 0, (size_t)p->desc.max_seqs * p->max_bps * sizeof(int32_t));
         if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->copy_stream, cudaStreamNonBlocking);
-        for (int i = 0; i < 4 && e == cudaSuccess; i++)
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->d2h_stream, cudaStreamNonBlocking);
+        for (int i = 0; i < 6 && e == cudaSuccess; i++)
             e = cudaEventCreateWithFlags(&p->io_ev[i], cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (e != cudaSuccess) {
@@ -485,6 +486,7 @@ int s1kv_pool_destroy(s1kv_pool* p) {
         for (auto& e : p->io_ev)
             if (e) cudaEventDestroy(e);
         if (p->copy_stream) cudaStreamDestroy(p->copy_stream);
+        if (p->d2h_stream) cudaStreamDestroy(p->d2h_stream);
     }
     delete p;
     return S1KV_OK;
