@@ -276,7 +276,7 @@ __global__ void quantize_rows_kernel(const float* __restrict__ w, int64_t rows, 
 }
 
 struct GemvShape {
-    int mb, cpl, cs, rows_per_cta, col_tiles, z;
+    int mb, cpl, cs, rows_per_cta, z;
     size_t smem;
 };
 
@@ -330,8 +330,7 @@ int launch_gemv(const float* x, int M, int K, GemvGroup grp, const GemvShape& g,
 //     bytes for up to 2 rows, 8 for 4; 4 rows per slice beat 8 here) and
 //     the fewest K splits, at most 512 rows per CTA: long row segments
 //     stream best and there are CTAs enough.
-static int gemv_shape(int M, int K, int N, int sms, int cap, GemvShape* g) {
-    (void)sms;
+static int gemv_shape(int M, int K, int N, int cap, GemvShape* g) {
     const bool wide = N >= 16384;
     g->mb = M >= 8 && !wide ? 8 : M >= 4 ? 4 : M >= 2 ? 2 : 1;
     g->z = (M + g->mb - 1) / g->mb;
@@ -344,7 +343,6 @@ static int gemv_shape(int M, int K, int N, int sms, int cap, GemvShape* g) {
         return set_error(S1KV_EINVAL, "matmul_int8: K = %d above %d", K, kMaxRowsCta * cap);
     g->cs = cs;
     const int nc = 32 * g->cpl;
-    g->col_tiles = (N + nc - 1) / nc;
     const int per_cta = (K + cs - 1) / cs;
     g->rows_per_cta = (per_cta + kGemvWarps - 1) / kGemvWarps * kGemvWarps;
     g->smem = sizeof(float) * ((size_t)g->mb * g->rows_per_cta + (size_t)(kGemvWarps + 1) * g->mb * nc);
@@ -400,7 +398,6 @@ static int matmul_int8_group(const float* x, int64_t M, int64_t K, int32_t n, co
     if (n < 1 || n > kMaxGroup) return set_error(S1KV_EINVAL, "matmul_int8: 1 to %d matrices per launch", kMaxGroup);
     if (M < 0 || K < 0 || M > (1 << 30) || K > (1 << 30)) return set_error(S1KV_EINVAL, "matmul_int8: bad shape");
     GemvGroup grp = {};
-    int64_t total_n = 0;
     for (int i = 0; i < n; i++) {
         if (N[i] < 0 || N[i] > (1 << 30)) return set_error(S1KV_EINVAL, "matmul_int8: bad shape");
         if (M > 0 && N[i] > 0 && (!x || !q[i] || !scales[i] || !out[i]))
@@ -411,7 +408,6 @@ static int matmul_int8_group(const float* x, int64_t M, int64_t K, int32_t n, co
         grp.m[grp.n].out = out[i];
         grp.m[grp.n].N = (int)N[i];
         grp.n++;
-        total_n += N[i];
     }
     if (M == 0 || grp.n == 0) return S1KV_OK;
     if (K == 0) {
@@ -419,16 +415,14 @@ static int matmul_int8_group(const float* x, int64_t M, int64_t K, int32_t n, co
             S1KV_CUDA(cudaMemsetAsync(grp.m[i].out, 0, sizeof(float) * (size_t)M * (size_t)grp.m[i].N, s));
         return S1KV_OK;
     }
-    int dev = 0, sms = 148;
+    int dev = 0;
     S1KV_CUDA(cudaGetDevice(&dev));
-    S1KV_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     GemvShape g;
     // the shape follows the group's widest matrix (narrow or wide loads)
     int widest = 0;
     for (int i = 0; i < grp.n; i++) widest = std::max(widest, grp.m[i].N);
-    int st = gemv_shape((int)M, (int)K, widest, sms, gemv_cluster_cap(dev), &g);
+    int st = gemv_shape((int)M, (int)K, widest, gemv_cluster_cap(dev), &g);
     if (st) return st;
-    (void)total_n;
     const int Mi = (int)M, Ki = (int)K;
 #define S1KV_GEMV(MB_, CPL_) \
     if (g.mb == MB_ && g.cpl == CPL_) return launch_gemv<MB_, CPL_>(x, Mi, Ki, grp, g, s);
