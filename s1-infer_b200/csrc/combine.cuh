@@ -17,12 +17,13 @@ __device__ __forceinline__ void store_out(const AttnParams& p, int64_t row, int 
 // Called by every thread of a CTA that has just stored a finished (row, KV
 // head): when the launch's last such CTA arrives, this rank's flag on every
 // rank is set to the epoch (release, system scope), after every store of the
-// launch (each CTA fences before arriving).
+// launch.  The barrier orders the CTA's stores before thread 0's system-scope
+// fence, which is cumulative over them (the pattern of a grid barrier).
 __device__ __forceinline__ void signal_done(const AttnParams& p) {
     if (!p.done) return;
-    __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
+        __threadfence_system();
         const uint32_t prev = atomicAdd(p.done, 1u);
         if (prev == (uint32_t)p.done_total - 1) {
             *p.done = 0;
@@ -121,15 +122,22 @@ __device__ __forceinline__ void combine_partials_staged(const AttnParams& p, int
 // CTA arrives, also after a timeout, so the counters always return to zero.
 __device__ __forceinline__ void finish_split_row(const AttnParams& p, int row, int h, int n_split, int G, int D,
                                                  int* flag, float* scratch, int scratch_floats) {
-    __threadfence();  // this CTA's partial is visible before its arrival
+    // One thread fences for the CTA (the pattern of a grid barrier): the
+    // barrier orders every thread's partial stores before thread 0's fence,
+    // which is cumulative over them, so the partial is visible before the
+    // arrival; the last arriver fences again before the merge reads (__ldcg,
+    // L2) and the barrier passes that on.  A fence in every thread made each
+    // CTA's exit wait for all of its threads' fences.
     __syncthreads();
     if (threadIdx.x == 0) {
+        __threadfence();
         const int prev = atomicAdd(&p.counters[(int64_t)row * p.Hkv + h], 1);
-        *flag = (prev == n_split - 1);
+        const bool last = prev == n_split - 1;
+        if (last) __threadfence();
+        *flag = last;
     }
     __syncthreads();
     if (*flag) {
-        __threadfence();  // every other CTA's partial is visible to this one
         if (2 * (n_split + 1) * G <= scratch_floats)
             combine_partials_staged(p, row, h, G, D, scratch);
         else
