@@ -565,12 +565,13 @@ int tma_warps_per_cta(int dtype, int D) {
 template <typename T, int D, int G>
 static int launch_decode_t(s1kv_pool* pool, const AttnParams& p, cudaStream_t stream) {
     using C = DecodeCfg<T, D, G>;
-    static bool attr_set = false;
-    if (!attr_set) {
+    static uint64_t attr_set = 0;  // per device
+    int st = once_per_device(attr_set, [] {
         S1KV_CUDA(cudaFuncSetAttribute(decode_tma_kernel<T, D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::kSmem));
-        attr_set = true;
-    }
+        return S1KV_OK;
+    });
+    if (st) return st;
     dim3 grid((unsigned)p.n_items, (unsigned)p.Hkv);
     decode_tma_kernel<T, D, G><<<grid, C::kNW * 32, C::kSmem, stream>>>(p, pool->tmap_k, pool->tmap_v);
     g_launches++;

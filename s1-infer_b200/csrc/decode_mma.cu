@@ -346,11 +346,12 @@ bool decode_mma_supported(int dtype, int D, int G, int block_size) {
 
 template <int G>
 static int launch_mma_g(const AttnParams& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream) {
-    static bool attr_set = false;
-    if (!attr_set) {
+    static uint64_t attr_set = 0;  // per device
+    int st = once_per_device(attr_set, [] {
         S1KV_CUDA(cudaFuncSetAttribute(decode_mma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
-        attr_set = true;
-    }
+        return S1KV_OK;
+    });
+    if (st) return st;
     dim3 grid((unsigned)p.n_items, (unsigned)p.Hkv);
     decode_mma_kernel<G><<<grid, kNW * 32, kSmem, stream>>>(p, tk, tv);
     g_launches++;

@@ -283,12 +283,13 @@ struct GemvShape {
 template <int MB, int CPL>
 int launch_gemv(const float* x, int M, int K, GemvGroup grp, const GemvShape& g, cudaStream_t stream) {
     auto kern = matmul_int8_kernel<MB, CPL>;
-    static bool attrs_set = false;
-    if (!attrs_set) {
+    static uint64_t attrs_set = 0;  // per device
+    int st = once_per_device(attrs_set, [&] {
         S1KV_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         S1KV_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemMax));
-        attrs_set = true;
-    }
+        return S1KV_OK;
+    });
+    if (st) return st;
     int tiles = 0;
     for (int i = 0; i < grp.n; i++) {
         GemvMat& m = grp.m[i];

@@ -46,6 +46,21 @@ struct DeviceGuard {
     DeviceGuard(const DeviceGuard&) = delete;
     DeviceGuard& operator=(const DeviceGuard&) = delete;
 };
+// Kernel attributes (dynamic shared memory, cluster size) belong to one
+// device's context: a process that drives several GPUs sets them on each.
+// `mask` holds one bit per device already set (devices 0-63).
+template <typename F>
+inline int once_per_device(uint64_t& mask, F&& set) {
+    int dev = 0;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+    const uint64_t bit = dev < 64 ? (uint64_t)1 << dev : 0;
+    if (bit && (mask & bit)) return 0;
+    const int st = set();
+    if (st == 0) mask |= bit;
+    return st;
+}
+
 #define S1KV_ON_DEVICE(dev)                                            \
     ::s1kv::DeviceGuard s1kv_device_guard_(dev);                       \
     if (s1kv_device_guard_.err != cudaSuccess) return ::s1kv::cuda_error(s1kv_device_guard_.err, "cudaSetDevice")
