@@ -802,7 +802,8 @@ def run_ours(args):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))  # each rank names its GPU
     share = contexts(world)[rank]
     peak, peak_kind = load_peaks()
     res = {}

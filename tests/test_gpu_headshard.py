@@ -31,7 +31,7 @@ def _rank(rank, world, port, out_dir):
     import s1kv
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=60))
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
     Hq, Hkv, D, bs = 32, 8, 128, 16
     ctx = [300, 517, 1024]
     B = len(ctx)
@@ -88,7 +88,7 @@ def _rank_fused(rank, world, port, out_dir):
     import s1kv
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=60))
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
     Hq, Hkv, D, bs = 32, 8, 128, 16
     ctx = [300, 517, 1024]
     B = len(ctx)
