@@ -166,6 +166,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) matmul_int8_kernel(const floa
     const int ka = k0 + tid, kb = k0 + tid + kGemvThreads;  // this thread's staged rows
     const float sa = tid < rows_per_cta && ka < K ? __ldg(scales + ka) : 0.0f;
     const float sb = tid + kGemvThreads < rows_per_cta && kb < K ? __ldg(scales + kb) : 0.0f;
+    // The next grid may launch as soon as every CTA of this one has got this
+    // far (all of them resident), and request its own weights while this one
+    // runs; it still waits for this grid to finish before reading its x.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     // x (written by the previous kernel) times the scale, 0 past K or M
 #pragma unroll
@@ -211,8 +215,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) matmul_int8_kernel(const floa
             }
         }
     }
-    // this CTA's weights are consumed: the next kernel may start its loads
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 #pragma unroll
     for (int m = 0; m < MB; m++)
 #pragma unroll
