@@ -27,10 +27,10 @@
 //     columns through distributed shared memory, in rank order.  One launch,
 //     no workspace, no atomics, the same result on every run.
 //   * Launched as a programmatic dependent launch: weights and scales never
-//     depend on the previous kernel, so a CTA requests its first weights,
-//     then waits for the previous grid (griddepcontrol.wait) before reading
-//     x, and lets the next grid launch once its own weights are consumed.
-//     Back-to-back projections overlap their launch and weight latency.
+//     depend on the previous kernel, so a CTA requests its first weights and
+//     its scales, lets the next grid launch, and only then waits for the
+//     previous grid (griddepcontrol.wait) before reading x.  Back-to-back
+//     projections overlap their launch and weight latency.
 //   * The sum over k is not in the reference's sequential order: results
 //     agree to within 2e-5 of the output scale (fp32), not bit for bit.
 //     Quantization is bit-exact (IEEE division, round half away from zero).
