@@ -310,6 +310,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int prefix = sm.kv_len - sm.q_len;
     const int kv_end = min(sm.kv_len, prefix + q0 + 2 * QT);  // tokens the last query may see
     const int n_tiles = (kv_end + kN - 1) / kN;
+    // the last chunk of a sequence may hold no query of tile B: its MMAs and
+    // softmax are skipped (uniform over the CTA)
+    const bool two_tiles = q0 + QT < sm.q_len;
     const int32_t* tab = p.table + (int64_t)sm.table_row * p.max_bps;
 
     // ---- set-up ----
@@ -433,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (ok) {
                 tc_fence_after();
                 issue_s(0, 0);
-                issue_s(1, 0);
+                if (two_tiles) issue_s(1, 0);
                 mma_commit_w(&k_empty[0]);
             }
             for (int t = 0; t < n_tiles && ok; t++) {
@@ -454,17 +457,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!ok) break;
                     issue_s(0, t + 1);
                 }
-                ok = warp_wait(&p_lo[1], (uint32_t)(t & 1), abort_flag);
-                if (!ok) break;
-                tc_fence_after();
-                issue_pv_half(1, t, 0);
-                ok = warp_wait(&p_full[1], (uint32_t)(t & 1), abort_flag);
-                if (!ok) break;
-                tc_fence_after();
-                issue_pv_half(1, t, 1);
-                mma_commit_w(&v_empty[slot]);
+                if (two_tiles) {
+                    ok = warp_wait(&p_lo[1], (uint32_t)(t & 1), abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_pv_half(1, t, 0);
+                    ok = warp_wait(&p_full[1], (uint32_t)(t & 1), abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_pv_half(1, t, 1);
+                }
+                mma_commit_w(&v_empty[slot]);  // after the last MMA that reads the stage
                 if (more) {
-                    issue_s(1, t + 1);
+                    if (two_tiles) issue_s(1, t + 1);
                     mma_commit_w(&k_empty[ns]);
                 }
             }
@@ -484,7 +489,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float m = -INFINITY;  // reference max (lags the true max by < 2^8)
         float l = 0.0f;
         bool ok = true;
-        for (int t = 0; t < n_tiles; t++) {
+        const bool active = X == 0 || two_tiles;  // an empty tile B does nothing
+        for (int t = 0; active && t < n_tiles; t++) {
             // S_X(t) done also means PV_X(t-1) done (tcgen05.commit tracks every
             // earlier MMA of the issuing thread): O_X and P_X are free.
             if (!warp_wait(&s_full[X], (uint32_t)(t & 1), abort_flag)) {
@@ -567,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         // last PV of this tile, then the output rows
-        if (ok && warp_wait(&pv_done[X], (uint32_t)((n_tiles - 1) & 1), abort_flag)) {
+        if (active && ok && warp_wait(&pv_done[X], (uint32_t)((n_tiles - 1) & 1), abort_flag)) {
             tc_fence_after();
             const float inv = 1.0f / l;
             if (q0 + 2 * QT <= sm.q_len) {
