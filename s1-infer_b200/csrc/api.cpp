@@ -503,6 +503,17 @@ int s1kv_batch_layer_host(s1kv_batch* b, int32_t layer, const float* h_q, const 
     const int s = b->io_calls++ & 1;
     char* d = (char*)p->io.p + s * slot_bytes;
     cudaEvent_t in_ready = p->io_ev[s], slot_done = p->io_ev[2 + s], out_done = p->io_ev[4 + s];
+    if (slot_bytes != p->io_slot_bytes) {
+        // the slots moved: this slot may overlap either slot of earlier calls,
+        // so wait for both before touching it
+        for (int o = 0; o < 2; o++)
+            if (p->io_slot_used[o]) {
+                S1KV_CUDA(cudaStreamWaitEvent(p->copy_stream, p->io_ev[2 + o], 0));
+                S1KV_CUDA(cudaStreamWaitEvent(p->copy_stream, p->io_ev[4 + o], 0));
+                S1KV_CUDA(cudaStreamWaitEvent(stream, p->io_ev[4 + o], 0));
+            }
+        p->io_slot_bytes = slot_bytes;
+    }
     if (p->io_slot_used[s]) S1KV_CUDA(cudaStreamWaitEvent(p->copy_stream, slot_done, 0));  // inputs consumed
     if (qb) S1KV_CUDA(cudaMemcpyAsync(d + oq, h_q, qb, cudaMemcpyHostToDevice, p->copy_stream));
     if (kb) {

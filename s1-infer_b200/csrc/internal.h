@@ -276,6 +276,7 @@ struct s1kv_pool {
     cudaStream_t d2h_stream = nullptr;
     cudaEvent_t io_ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
     bool io_slot_used[2] = {false, false};
+    size_t io_slot_bytes = 0;          // slot size of the last call (slots move when it changes)
 };
 
 // Peer exchange of attention outputs for KV-head sharding (exchange.cu).
