@@ -212,9 +212,11 @@ def run_variant(s1kv, torch, dtype, ctx, steps, warmup, rank, world, timed_e2e, 
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push(f"timed_decode_{dtype}")  # ncu --nvtx-include filters the launch list on it
     t0.record()
+    h0 = time.perf_counter()
     for i in range(steps):
         step(evs[i])
     t1.record()
+    host_ms = (time.perf_counter() - h0) * 1e3  # issuing the steps; below the device time: not host-bound
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_pop()
     launches = s1kv.launch_count() - launches0
@@ -233,6 +235,7 @@ def run_variant(s1kv, torch, dtype, ctx, steps, warmup, rank, world, timed_e2e, 
         "clocks": clk,
         "tokens": B * steps,
         "kv_bytes_step": attn_bytes / steps,
+        "host_issue_ms_per_step": host_ms / steps,
     }
     if timed_e2e:
         hq = torch.empty((LAYERS, B, HQ, D), pin_memory=True)
@@ -881,6 +884,7 @@ def run_ours(args):
                 "d2h_bytes_per_step": h["d2h_bytes_per_step"],
                 "path": "s1kv_batch_layer_host (C ABI, pinned host buffers, copies in the timed region)"},
         "gpu_launches": h["launches"],
+        "host_issue_ms_per_step": h["host_issue_ms_per_step"],
         "clocks": h["clocks"],
         "variants": {"bf16_kv": {
             "value": bf_tokens / (bf_elapsed * 1e-3), "unit": "tok/s",
