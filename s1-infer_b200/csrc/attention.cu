@@ -565,7 +565,7 @@ int tma_warps_per_cta(int dtype, int D) {
 template <typename T, int D, int G>
 static int launch_decode_t(s1kv_pool* pool, const AttnParams& p, cudaStream_t stream) {
     using C = DecodeCfg<T, D, G>;
-    static uint64_t attr_set = 0;  // per device
+    static std::atomic<uint64_t> attr_set{0};  // per device
     int st = once_per_device(attr_set, [] {
         S1KV_CUDA(cudaFuncSetAttribute(decode_tma_kernel<T, D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::kSmem));

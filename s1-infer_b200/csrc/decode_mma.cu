@@ -346,7 +346,7 @@ bool decode_mma_supported(int dtype, int D, int G, int block_size) {
 
 template <int G>
 static int launch_mma_g(const AttnParams& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream) {
-    static uint64_t attr_set = 0;  // per device
+    static std::atomic<uint64_t> attr_set{0};  // per device
     int st = once_per_device(attr_set, [] {
         S1KV_CUDA(cudaFuncSetAttribute(decode_mma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
         return S1KV_OK;

@@ -285,7 +285,7 @@ struct GemvShape {
 template <int MB, int CPL>
 int launch_gemv(const float* x, int M, int K, GemvGroup grp, const GemvShape& g, cudaStream_t stream) {
     auto kern = matmul_int8_kernel<MB, CPL>;
-    static uint64_t attrs_set = 0;  // per device
+    static std::atomic<uint64_t> attrs_set{0};  // per device
     int st = once_per_device(attrs_set, [&] {
         S1KV_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         S1KV_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemMax));
@@ -355,9 +355,9 @@ static int gemv_shape(int M, int K, int N, int cap, GemvShape* g) {
 // Largest cluster along K this device co-schedules for the kernel: 16 (a
 // non-portable size) where the occupancy query allows it, else 8.
 static int gemv_cluster_cap(int dev) {
-    static int cap[64] = {0};
+    static std::atomic<int> cap[64];  // 0 = not yet queried
     if (dev < 0 || dev >= 64) return 8;
-    if (cap[dev]) return cap[dev];
+    if (const int c = cap[dev].load(std::memory_order_acquire)) return c;
     auto kern = matmul_int8_kernel<8, 4>;
     int n = 0;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
@@ -376,8 +376,9 @@ static int gemv_cluster_cap(int dev) {
         if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
     }
     cudaGetLastError();  // a refused query leaves no error behind
-    cap[dev] = n > 0 ? kMaxCluster : 8;
-    return cap[dev];
+    const int c = n > 0 ? kMaxCluster : 8;
+    cap[dev].store(c, std::memory_order_release);
+    return c;
 }
 
 }  // namespace s1kv

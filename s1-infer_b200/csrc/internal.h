@@ -48,16 +48,17 @@ struct DeviceGuard {
 };
 // Kernel attributes (dynamic shared memory, cluster size) belong to one
 // device's context: a process that drives several GPUs sets them on each.
-// `mask` holds one bit per device already set (devices 0-63).
+// `mask` holds one bit per device already set (devices 0-63); setting an
+// attribute twice from racing threads is harmless, the mask is atomic.
 template <typename F>
-inline int once_per_device(uint64_t& mask, F&& set) {
+inline int once_per_device(std::atomic<uint64_t>& mask, F&& set) {
     int dev = 0;
     const cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
     const uint64_t bit = dev < 64 ? (uint64_t)1 << dev : 0;
-    if (bit && (mask & bit)) return 0;
+    if (bit && (mask.load(std::memory_order_acquire) & bit)) return 0;
     const int st = set();
-    if (st == 0) mask |= bit;
+    if (st == 0) mask.fetch_or(bit, std::memory_order_acq_rel);
     return st;
 }
 
