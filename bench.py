@@ -37,6 +37,7 @@ for _p in (ROOT, os.path.join(ROOT, "s1-infer_b200")):
 
 METRIC = "paged decode-attn KV GB/s/GPU (% HBM peak); decode tok/s at 1/2/4/8 B200"
 LAYERS, HQ, HKV, D, BS = 32, 32, 8, 128, 16  # LAYERS may be lowered by --layers for profiling cases
+EVENT_STEPS = 5  # decode steps of the per-launch timing pass that follows the timed steps
 SEQS_PER_GPU = 64
 CTX_LO, CTX_HI, CTX_SEED = 128, 4096, 1
 WORKLOAD = "cfg2: batched ragged paged decode, Llama-3-8B attention shape"
@@ -166,7 +167,7 @@ class ClockSampler:
 def run_variant(s1kv, torch, dtype, ctx, steps, warmup, rank, world, timed_e2e, sample_clocks):
     elem = 4 if dtype == "f32" else 2
     B = len(ctx)
-    total_steps = 2 * (steps + warmup) + 2
+    total_steps = 2 * (steps + warmup) + min(steps, EVENT_STEPS) + 2
     need = sum((c + total_steps + BS - 1) // BS for c in ctx)
     max_blocks = int(need * 1.25)
     rng = np.random.default_rng(1000 + rank)
@@ -206,9 +207,7 @@ def run_variant(s1kv, torch, dtype, ctx, steps, warmup, rank, world, timed_e2e, 
         step()
     barrier(torch, world)
     torch.cuda.synchronize()
-    ctx_before = [pool.length(s) for s in seqs]
-    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(LAYERS)]
-           for _ in range(steps)]
+    ctx_timed = [pool.length(s) for s in seqs]
     clocks = ClockSampler(torch.cuda.current_device()) if sample_clocks else None
     if clocks:
         clocks.start()
@@ -218,7 +217,7 @@ def run_variant(s1kv, torch, dtype, ctx, steps, warmup, rank, world, timed_e2e, 
     t0.record()
     h0 = time.perf_counter()
     for i in range(steps):
-        step(evs[i])
+        step()
     t1.record()
     host_ms = (time.perf_counter() - h0) * 1e3  # issuing the steps; below the device time: not host-bound
     torch.cuda.synchronize()
@@ -226,8 +225,19 @@ def run_variant(s1kv, torch, dtype, ctx, steps, warmup, rank, world, timed_e2e, 
     launches = s1kv.launch_count() - launches0
     clk = clocks.stop() if clocks else None
     elapsed_ms = t0.elapsed_time(t1)
-    attn_ms = [evs[i][layer][0].elapsed_time(evs[i][layer][1]) for i in range(steps) for layer in range(LAYERS)]
-    attn_bytes = sum(decode_bytes([c + i + 1 for c in ctx_before], elem) for i in range(steps)) * LAYERS
+    # Attention launch durations: the next steps again with an event pair
+    # around every attention call.  An event recorded between two kernels
+    # ends the programmatic overlap of their launches, so the timed steps
+    # above carry no per-layer events.
+    n_ev = min(steps, EVENT_STEPS)
+    ctx_before = [pool.length(s) for s in seqs]
+    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(LAYERS)]
+           for _ in range(n_ev)]
+    for i in range(n_ev):
+        step(evs[i])
+    torch.cuda.synchronize()
+    attn_ms = [evs[i][layer][0].elapsed_time(evs[i][layer][1]) for i in range(n_ev) for layer in range(LAYERS)]
+    attn_bytes = sum(decode_bytes([c + i + 1 for c in ctx_before], elem) for i in range(n_ev)) * LAYERS
     res = {
         "elapsed_ms": elapsed_ms,
         "attn_ms_total": float(sum(attn_ms)),
@@ -238,7 +248,7 @@ def run_variant(s1kv, torch, dtype, ctx, steps, warmup, rank, world, timed_e2e, 
         "launches": launches,
         "clocks": clk,
         "tokens": B * steps,
-        "kv_bytes_step": attn_bytes / steps,
+        "kv_bytes_step": sum(decode_bytes([c + i + 1 for c in ctx_timed], elem) for i in range(steps)) * LAYERS / steps,
         "host_issue_ms_per_step": host_ms / steps,
     }
     if timed_e2e:
@@ -883,7 +893,9 @@ def run_ours(args):
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
                      else "fallback 6650 GB/s", "bytes_per_launch": h["bytes_per_launch"],
-                     "avg_launch_ms": h["avg_launch_ms"], "traffic": None},
+                     "avg_launch_ms": h["avg_launch_ms"], "traffic": None,
+                     "timing": f"CUDA events around each attention call over {min(args.steps, EVENT_STEPS)} decode "
+                               "steps run right after the timed steps"},
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h["h2d_bytes_per_step"],
                 "d2h_bytes_per_step": h["d2h_bytes_per_step"],
                 "path": "s1kv_batch_layer_host (C ABI, pinned host buffers, copies in the timed region)"},

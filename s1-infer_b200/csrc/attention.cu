@@ -241,6 +241,7 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, 
     constexpr int NW = C::kNW, NS = C::kNS, NV = C::kNV, LPT = C::kLPT, IT = C::kIT, EPC = C::kEPC,
                   TPS = C::kTPS, STEPS = C::kSteps, DPL = C::kDPL, DQ = C::kDQ, TILE = C::kTile;
     extern __shared__ __align__(1024) uint8_t smem[];
+    pdl_enter();
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = blockIdx.y;
@@ -573,7 +574,8 @@ static int launch_decode_t(s1kv_pool* pool, const AttnParams& p, cudaStream_t st
     });
     if (st) return st;
     dim3 grid((unsigned)p.n_items, (unsigned)p.Hkv);
-    decode_tma_kernel<T, D, G><<<grid, C::kNW * 32, C::kSmem, stream>>>(p, pool->tmap_k, pool->tmap_v);
+    S1KV_CUDA(launch_pdl(decode_tma_kernel<T, D, G>, grid, dim3(C::kNW * 32), C::kSmem, stream, p, pool->tmap_k,
+                         pool->tmap_v));
     g_launches++;
     S1KV_CUDA(cudaGetLastError());
     if (!p.counters) {  // otherwise the last CTA of each split row merged it; combine exits early for single-split rows

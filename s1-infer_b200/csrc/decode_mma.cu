@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
                       const __grid_constant__ CUtensorMap tmV) {
     static_assert(G >= 1 && G <= 8, "query heads per KV head must fit the 8 live rows of an m16 tile");
     extern __shared__ uint8_t smem_raw[];
+    pdl_enter();
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;  // mma fragment coordinates: head row, column pair
@@ -353,7 +354,7 @@ static int launch_mma_g(const AttnParams& p, const CUtensorMap& tk, const CUtens
     });
     if (st) return st;
     dim3 grid((unsigned)p.n_items, (unsigned)p.Hkv);
-    decode_mma_kernel<G><<<grid, kNW * 32, kSmem, stream>>>(p, tk, tv);
+    S1KV_CUDA(launch_pdl(decode_mma_kernel<G>, grid, dim3(kNW * 32), kSmem, stream, p, tk, tv));
     g_launches++;
     S1KV_CUDA(cudaGetLastError());
     return S1KV_OK;

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <utility>
 #include <cstdint>
 #include <list>
 #include <string>
@@ -61,6 +62,34 @@ inline int once_per_device(std::atomic<uint64_t>& mask, F&& set) {
     if (st == 0) mask.fetch_or(bit, std::memory_order_acq_rel);
     return st;
 }
+
+// Programmatic dependent launch of the step's chain of kernels (RoPE +
+// append, decode attention): a kernel launched with launch_pdl may become
+// resident while the previous kernel of the stream finishes; pdl_enter at
+// its very top lets the next kernel do the same and then waits for the
+// previous grid to complete (its memory visible) before this one reads
+// anything.  Without the launch attribute the wait returns at once.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+#ifdef __CUDACC__
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+#endif
 
 #define S1KV_ON_DEVICE(dev)                                            \
     ::s1kv::DeviceGuard s1kv_device_guard_(dev);                       \

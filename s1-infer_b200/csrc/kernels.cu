@@ -141,6 +141,7 @@ __device__ __forceinline__ void rotate8(float* x1, float* x2, const float2* cs) 
 
 template <typename T, bool ROPE>
 __global__ void __launch_bounds__(256) append_vec_kernel(const AppendParams p) {
+    pdl_enter();
     const int D = p.D, half = D / 2;
     const int upr = half / 8;  // units per (token, head)
     const int64_t kv_units = p.n * p.Hkv * upr;
@@ -197,6 +198,7 @@ __global__ void __launch_bounds__(256) append_vec_kernel(const AppendParams p) {
 // unaligned inputs (the reference's own tests use head_dim 1 and 2).
 template <typename T, bool ROPE>
 __global__ void append_scalar_kernel(const AppendParams p) {
+    pdl_enter();
     const int D = p.D, half = D / 2;
     const int64_t kv_elems = p.n * p.Hkv * D;
     const int64_t q_elems = (ROPE && p.q_in) ? p.n * p.Hq * D : 0;
@@ -249,9 +251,9 @@ int launch_append(const AppendParams& p, int dtype, bool rope, cudaStream_t stre
     int64_t units = vec ? (2 * p.n * p.Hkv + (rope && p.q_in ? p.n * p.Hq : 0)) * (p.D / 16)
                         : (2 * p.n * p.Hkv + (rope && p.q_in ? p.n * p.Hq : 0)) * p.D;
     int grid = (int)std::max<int64_t>(1, std::min<int64_t>((units + 255) / 256, kSMs * 16));
-#define S1KV_APPEND(T, R)                                                                      \
-    (vec ? (void)append_vec_kernel<T, R><<<grid, 256, 0, stream>>>(p)                           \
-         : (void)append_scalar_kernel<T, R><<<grid, 256, 0, stream>>>(p))
+#define S1KV_APPEND(T, R)                                                                                    \
+    S1KV_CUDA(vec ? launch_pdl(append_vec_kernel<T, R>, dim3(grid), dim3(256), 0, stream, p)                    \
+                  : launch_pdl(append_scalar_kernel<T, R>, dim3(grid), dim3(256), 0, stream, p))
     if (dtype == S1KV_DTYPE_F32) {
         if (rope) S1KV_APPEND(float, true);
         else S1KV_APPEND(float, false);
