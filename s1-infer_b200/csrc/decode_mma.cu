@@ -13,21 +13,23 @@
 // Why tensor cores for an HBM-bound kernel: with 8 query heads per KV head
 // every K/V element feeds 8 multiply-adds plus a bf16 widening, which makes
 // the CUDA-core kernel issue-bound well below the HBM roofline.  Here one
-// 16-token tile costs 16 ldmatrix and 64 mma instructions per warp.
-//   * S[head, token] = Q K^T: M = query heads of the group (padded to 16,
-//     rows >= G are zero), N = 8 tokens, K = 16 dims.  K tiles arrive by
-//     TMA in the 128-byte-swizzled layout (two 64-element halves per row),
-//     so ldmatrix reads them without bank conflicts.
-//   * The score fragment of a thread (head g, tokens 2t, 2t+1, 2t+8, 2t+9)
-//     is exactly its A fragment of O += P V, so P never leaves registers;
-//     V fragments come from ldmatrix.trans.
+// 16-token tile costs 16 ldmatrix, 4 movmatrix and 32 mma per warp.
+//   * Token-major products, so the 8 heads (or fewer) of a group fill the
+//     N = 8 side of m16n8k16 and no M rows are padding:
+//     S^T[token, head] = K Q^T with M = 16 tokens, K = 16 dims; K tiles
+//     arrive by TMA in the 128-byte-swizzled layout (two 64-element halves
+//     per row), so ldmatrix reads them without bank conflicts.
+//   * The score fragment of a thread (tokens g, g+8; heads 2t, 2t+1) turns
+//     into P's B fragment of O^T += V^T P^T (head g; tokens 2t, 2t+1,
+//     2t+8, 2t+9) by one movmatrix transpose per 8x8 half, so P never
+//     leaves registers; V^T fragments come from ldmatrix.trans.
 //   * Precision: q (fp32, pre-scaled by log2(e)/sqrt(D)) and p are each
 //     split into bf16 hi + lo parts and both parts are multiplied (K and V
 //     are exact in bf16), so scores and outputs carry fp32-level error
 //     (about 2^-17 relative), not bf16 error.
-//   * Online softmax in the exp2 domain per head, replicated over the 4
-//     lanes of a head; the reference max moves only when a tile's max
-//     outgrows it by 2^8, and only then is that head's O rescaled.
+//   * Online softmax in the exp2 domain per head (a column held by 8
+//     lanes); the reference max moves only when a tile's max outgrows it
+//     by 2^8, and only then is the max reduced and that head's O rescaled.
 // Waits are bounded (device error word on timeout, copies drained).
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -45,8 +47,8 @@ constexpr uint32_t kSpin = 1u << 22;
 constexpr int kD = 128;
 constexpr int kTile = 16;                      // tokens per stage (one block)
 constexpr int kNW = 4;                         // warps per CTA
-constexpr int kNS = 3;                         // stages per warp
-constexpr int kMinCtas = 2;
+constexpr int kNS = 2;                         // stages per warp
+constexpr int kMinCtas = 3;
 constexpr int kBoxBytes = kTile * 128;         // 16 tokens x 64 bf16, 128B-swizzled
 constexpr int kTileBytes = 2 * kBoxBytes;      // K (or V) of one tile: 4 KB
 constexpr int kStageBytes = 2 * kTileBytes;    // K + V
@@ -93,13 +95,21 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
                  : "r"(addr));
 }
 
-// c += A B for one m16n8k16 tile; A rows 8..15 (padding heads) are zero.
-__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+// c += A B for one m16n8k16 tile (bf16 x bf16 -> fp32).
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
         "{%0, %1, %2, %3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Transpose of an 8x8 b16 matrix held as the warp's m8n8 fragment (lane L:
+// row L / 4, columns 2(L % 4), 2(L % 4) + 1).
+__device__ __forceinline__ uint32_t movt(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -178,9 +188,9 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
         if (lane == 0) issue(k, row);
     }
 
-    // A fragments of q (pre-scaled, split hi + lo): k-step ks covers dims
-    // 16ks .. 16ks+15; this lane holds dims 2tq, 2tq+1 (a0) and 2tq+8, 2tq+9
-    // (a2) of head gq.
+    // B fragments of q^T (pre-scaled, split hi + lo): k-step ks covers dims
+    // 16ks .. 16ks+15; this lane holds dims 2tq, 2tq+1 (b0) and 2tq+8, 2tq+9
+    // (b1) of head gq (zero for the padding heads gq >= G).
     uint32_t qh[kD / 16][2], ql[kD / 16][2];
     {
         const float* qrow = p.q + ((int64_t)item.row * p.Hq + h * G + (gq < G ? gq : 0)) * kD;
@@ -194,10 +204,15 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
             }
     }
 
-    float o[kD / 8][4];  // O[head gq][8nb + 2tq + {0,1}] in [nb][0..1]; [2..3] are padding rows
+    // O^T accumulators: m-block mb covers dims 16mb .. 16mb+15; [mb][0] and
+    // [mb][1] are dim 16mb + gq of heads 2tq and 2tq+1, [2] and [3] dim
+    // 16mb + gq + 8 of the same heads.
+    float o[kD / 16][4];
 #pragma unroll
-    for (int nb = 0; nb < kD / 8; nb++) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.0f;
-    float m = -INFINITY, l = 0.0f;  // head gq: reference max (log2 units), this lane's share of the sum
+    for (int mb = 0; mb < kD / 16; mb++) o[mb][0] = o[mb][1] = o[mb][2] = o[mb][3] = 0.0f;
+    // heads 2tq, 2tq+1: reference max (log2 units, the same in the 8 lanes of
+    // a head) and this lane's share of the sum (tokens gq, gq+8 of each tile)
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
 
     // ldmatrix row addresses: lane L supplies row (L & 7) of matrix L >> 3.
     const int mi = lane >> 3, r8 = lane & 7;
@@ -214,60 +229,76 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
         const int base = tok0 + (warp + k * kNW) * kTile;
         const int valid = min(kTile, tok1 - base);
 
-        // ---- S = Q K^T: n-block 0 = tokens 0-7, 1 = tokens 8-15 ----
-        float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+        // ---- S^T = K Q^T: M = the 16 tokens, N = the 8 head columns ----
+        // four accumulators (hi / lo part of q, even / odd k-step) keep the
+        // dependent chains four mma long
+        float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+        float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int ks = 0; ks < kD / 16; ks++) {
-            uint32_t b[4];  // matrix mi: tokens 8(mi >> 1) + r8, dims 16ks + 8(mi & 1) ..
-            ldsm_x4(tile_chunk(Kt, (mi >> 1) * 8 + r8, ks * 2 + (mi & 1)), b);
-            mma16816(s0, qh[ks][0], qh[ks][1], b[0], b[1]);
-            mma16816(s0, ql[ks][0], ql[ks][1], b[0], b[1]);
-            mma16816(s1, qh[ks][0], qh[ks][1], b[2], b[3]);
-            mma16816(s1, ql[ks][0], ql[ks][1], b[2], b[3]);
+        for (int ks = 0; ks < kD / 16; ks += 2) {
+            uint32_t a[4], a2[4];  // matrix mi: tokens 8(mi & 1) + r8, dims 16ks + 8(mi >> 1) ..
+            ldsm_x4(tile_chunk(Kt, (mi & 1) * 8 + r8, ks * 2 + (mi >> 1)), a);
+            ldsm_x4(tile_chunk(Kt, (mi & 1) * 8 + r8, (ks + 1) * 2 + (mi >> 1)), a2);
+            mma16816(sa, a, qh[ks][0], qh[ks][1]);
+            mma16816(sb, a, ql[ks][0], ql[ks][1]);
+            mma16816(sc, a2, qh[ks + 1][0], qh[ks + 1][1]);
+            mma16816(sd, a2, ql[ks + 1][0], ql[ks + 1][1]);
         }
-        // this lane: head gq, tokens 2tq, 2tq+1, 2tq+8, 2tq+9
-        float x[4] = {s0[0], s0[1], s1[0], s1[1]};
+        // this lane: [0] token gq head 2tq, [1] token gq head 2tq+1,
+        // [2] token gq+8 head 2tq, [3] token gq+8 head 2tq+1
+        float x[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) x[i] = (sa[i] + sc[i]) + (sb[i] + sd[i]);
         if (valid < kTile) {
-            if (2 * tq >= valid) x[0] = -INFINITY;
-            if (2 * tq + 1 >= valid) x[1] = -INFINITY;
-            if (2 * tq + 8 >= valid) x[2] = -INFINITY;
-            if (2 * tq + 9 >= valid) x[3] = -INFINITY;
+            if (gq >= valid) x[0] = x[1] = -INFINITY;
+            if (gq + 8 >= valid) x[2] = x[3] = -INFINITY;
         }
-        float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
-        const bool raise = mx > m + kRescaleAt;
-        if (__any_sync(kFull, raise)) {
-            const float corr = raise ? ex2(m - mx) : 1.0f;  // 0 on the first tile (m = -inf)
-            if (raise) {
-                m = mx;
-                l *= corr;
+        // the reference max of a head moves only when one of its scores
+        // outgrows it by 2^8; the head's max over the tile is reduced (over
+        // the 8 lanes of a column) only on such a tile
+        float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
+        if (__any_sync(kFull, mx0 > m0 + kRescaleAt || mx1 > m1 + kRescaleAt)) {
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, off));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, off));
+            }
+            const bool r0 = mx0 > m0 + kRescaleAt, r1 = mx1 > m1 + kRescaleAt;
+            const float c0 = r0 ? ex2(m0 - mx0) : 1.0f, c1 = r1 ? ex2(m1 - mx1) : 1.0f;  // 0 from m = -inf
+            if (r0) {
+                m0 = mx0;
+                l0 *= c0;
+            }
+            if (r1) {
+                m1 = mx1;
+                l1 *= c1;
             }
 #pragma unroll
-            for (int nb = 0; nb < kD / 8; nb++) {
-                o[nb][0] *= corr;
-                o[nb][1] *= corr;
+            for (int mb = 0; mb < kD / 16; mb++) {
+                o[mb][0] *= c0;
+                o[mb][1] *= c1;
+                o[mb][2] *= c0;
+                o[mb][3] *= c1;
             }
         }
-        float pr[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            pr[i] = ex2(x[i] - m);
-            l += pr[i];
-        }
-        uint32_t ph01, pl01, ph23, pl23;  // A fragment of P: tokens (2tq, 2tq+1) and (2tq+8, 2tq+9)
-        split_bf16(pr[0], pr[1], ph01, pl01);
-        split_bf16(pr[2], pr[3], ph23, pl23);
+        const float p0 = ex2(x[0] - m0), p1 = ex2(x[1] - m1), p2 = ex2(x[2] - m0), p3 = ex2(x[3] - m1);
+        l0 += p0 + p2;
+        l1 += p1 + p3;
+        // P^T fragments (token rows, head columns) in bf16 hi + lo, then
+        // transposed in registers into the B fragments of O^T += V^T P^T:
+        // head gq, tokens 2tq, 2tq+1 (b0) and 2tq+8, 2tq+9 (b1)
+        uint32_t h0, l0p, h1, l1p;
+        split_bf16(p0, p1, h0, l0p);
+        split_bf16(p2, p3, h1, l1p);
+        const uint32_t bh0 = movt(h0), bh1 = movt(h1), bl0 = movt(l0p), bl1 = movt(l1p);
 
-        // ---- O += P V: two n-blocks (16 dims) per ldmatrix.x4.trans ----
+        // ---- O^T += V^T P^T: M = 16 dims per m-block, K = the 16 tokens ----
 #pragma unroll
-        for (int nb2 = 0; nb2 < kD / 16; nb2++) {
-            uint32_t b[4];  // matrix mi: tokens 8(mi & 1) + r8, dims 16nb2 + 8(mi >> 1) ..
-            ldsm_x4_t(tile_chunk(Vt, (mi & 1) * 8 + r8, nb2 * 2 + (mi >> 1)), b);
-            mma16816(o[2 * nb2], ph01, ph23, b[0], b[1]);
-            mma16816(o[2 * nb2], pl01, pl23, b[0], b[1]);
-            mma16816(o[2 * nb2 + 1], ph01, ph23, b[2], b[3]);
-            mma16816(o[2 * nb2 + 1], pl01, pl23, b[2], b[3]);
+        for (int mb = 0; mb < kD / 16; mb++) {
+            uint32_t a[4];  // matrix mi: tokens 8(mi >> 1) + r8, dims 16mb + 8(mi & 1) .., transposed
+            ldsm_x4_t(tile_chunk(Vt, (mi >> 1) * 8 + r8, mb * 2 + (mi & 1)), a);
+            mma16816(o[mb], a, bh0, bh1);
+            mma16816(o[mb], a, bl0, bl1);
         }
         __syncwarp();
         if (k + kNS < my_tiles) {
@@ -288,25 +319,43 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
         if (lane == 0) atomicOr(p.err, kErrTimeout);
         const int issued = min(my_tiles, consumed + kNS);
         for (int k = consumed + 1; k < issued; k++) bar_wait(&bar[k % kNS], (uint32_t)((k / kNS) & 1));
-        m = -INFINITY;
-        l = 0.0f;
+        m0 = m1 = -INFINITY;
+        l0 = l1 = 0.0f;
 #pragma unroll
-        for (int nb = 0; nb < kD / 8; nb++) o[nb][0] = o[nb][1] = 0.0f;
+        for (int mb = 0; mb < kD / 16; mb++) o[mb][0] = o[mb][1] = o[mb][2] = o[mb][3] = 0.0f;
     }
-    l += __shfl_xor_sync(kFull, l, 1);
-    l += __shfl_xor_sync(kFull, l, 2);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        l0 += __shfl_xor_sync(kFull, l0, off);
+        l1 += __shfl_xor_sync(kFull, l1, off);
+    }
 
     // ---- merge the warps through shared memory (aliases the rings) ----
     __syncthreads();
     float* mo = reinterpret_cast<float*>(smem);  // [kNW][G][kD]
     float* mml = mo + kNW * G * kD;              // [kNW][G][2]
-    if (gq < G) {
+    if (2 * tq < G) {
+        float* dst = &mo[(warp * G + 2 * tq) * kD + gq];
 #pragma unroll
-        for (int nb = 0; nb < kD / 8; nb++)
-            *reinterpret_cast<float2*>(&mo[(warp * G + gq) * kD + nb * 8 + 2 * tq]) = make_float2(o[nb][0], o[nb][1]);
-        if (tq == 0) {
-            mml[(warp * G + gq) * 2] = m;
-            mml[(warp * G + gq) * 2 + 1] = l;
+        for (int mb = 0; mb < kD / 16; mb++) {
+            dst[16 * mb] = o[mb][0];
+            dst[16 * mb + 8] = o[mb][2];
+        }
+        if (gq == 0) {
+            mml[(warp * G + 2 * tq) * 2] = m0;
+            mml[(warp * G + 2 * tq) * 2 + 1] = l0;
+        }
+    }
+    if (2 * tq + 1 < G) {
+        float* dst = &mo[(warp * G + 2 * tq + 1) * kD + gq];
+#pragma unroll
+        for (int mb = 0; mb < kD / 16; mb++) {
+            dst[16 * mb] = o[mb][1];
+            dst[16 * mb + 8] = o[mb][3];
+        }
+        if (gq == 0) {
+            mml[(warp * G + 2 * tq + 1) * 2] = m1;
+            mml[(warp * G + 2 * tq + 1) * 2 + 1] = l1;
         }
     }
     __syncthreads();
