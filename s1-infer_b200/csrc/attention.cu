@@ -244,8 +244,10 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, 
     pdl_enter();
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.y;
-    const WorkItem item = p.items[blockIdx.x];
+    // CTA index = item * Hkv + head: the heads of one item run side by side
+    // and read the same token rows of the pool together
+    const int h = (int)(blockIdx.x % (unsigned)p.Hkv);
+    const WorkItem item = p.items[blockIdx.x / (unsigned)p.Hkv];
     const RowMeta rm = p.rows[item.row];
     const int tok0 = item.split * p.split_tokens;
     const int tok1 = min(tok0 + p.split_tokens, rm.kv_len);
@@ -573,7 +575,8 @@ static int launch_decode_t(s1kv_pool* pool, const AttnParams& p, cudaStream_t st
         return S1KV_OK;
     });
     if (st) return st;
-    dim3 grid((unsigned)p.n_items, (unsigned)p.Hkv);
+    if ((int64_t)p.n_items * p.Hkv > INT32_MAX) return set_error(S1KV_EINVAL, "decode: too many work items");
+    const dim3 grid((unsigned)((int64_t)p.n_items * p.Hkv));
     S1KV_CUDA(launch_pdl(decode_tma_kernel<T, D, G>, grid, dim3(C::kNW * 32), C::kSmem, stream, p, pool->tmap_k,
                          pool->tmap_v));
     g_launches++;
@@ -719,7 +722,8 @@ template <typename T, int D, int G>
 static int launch_with_maps_t(const AttnParams& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream) {
     using C = DecodeCfg<T, D, G>;
     S1KV_CUDA(cudaFuncSetAttribute(decode_tma_kernel<T, D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
-    decode_tma_kernel<T, D, G><<<dim3((unsigned)p.n_items, (unsigned)p.Hkv), C::kNW * 32, C::kSmem, stream>>>(p, tk, tv);
+    if ((int64_t)p.n_items * p.Hkv > INT32_MAX) return set_error(S1KV_EINVAL, "decode: too many work items");
+    decode_tma_kernel<T, D, G><<<dim3((unsigned)((int64_t)p.n_items * p.Hkv)), C::kNW * 32, C::kSmem, stream>>>(p, tk, tv);
     g_launches++;
     S1KV_CUDA(cudaGetLastError());
     combine_kernel<<<dim3((unsigned)p.n_rows, (unsigned)p.Hkv), 128, 0, stream>>>(p, G);
