@@ -38,6 +38,14 @@ for _p in (ROOT, os.path.join(ROOT, "s1-infer_b200")):
 METRIC = "paged decode-attn KV GB/s/GPU (% HBM peak); decode tok/s at 1/2/4/8 B200"
 LAYERS, HQ, HKV, D, BS = 32, 32, 8, 128, 16  # LAYERS may be lowered by --layers for profiling cases
 EVENT_STEPS = 5  # decode steps of the per-launch timing pass that follows the timed steps
+# DRAM bytes (read + write) per decode launch over its algorithmic bytes, from
+# one ncu capture of each kernel on the one- or two-layer case of this
+# workload (same shapes, 1.08 GB / 0.54 GB per launch, above L2):
+#   fp32 decode_tma_kernel: 1.081969 GB read + 5.774 MB written, 1.082991 GB algorithmic
+#   bf16 decode_mma_kernel: 0.542480 GB read + 7.267 MB written, 0.542561 GB algorithmic
+# Traffic grows with the context like the algorithmic bytes, so a launch of
+# the full run is reported as this ratio times its algorithmic bytes.
+DRAM_PER_ALGORITHMIC = {"f32": (1.081969e9 + 5.774e6) / 1.082991e9, "bf16": (0.542480e9 + 7.267e6) / 0.542561e9}
 SEQS_PER_GPU = 64
 CTX_LO, CTX_HI, CTX_SEED = 128, 4096, 1
 WORKLOAD = "cfg2: batched ragged paged decode, Llama-3-8B attention shape"
@@ -893,7 +901,10 @@ def run_ours(args):
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
                      else "fallback 6650 GB/s", "bytes_per_launch": h["bytes_per_launch"],
-                     "avg_launch_ms": h["avg_launch_ms"], "traffic": None,
+                     "avg_launch_ms": h["avg_launch_ms"],
+                     "traffic": DRAM_PER_ALGORITHMIC["f32"] * h["bytes_per_launch"],
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a one-layer capture, "
+                                       "scaled to this launch by its algorithmic bytes",
                      "timing": f"CUDA events around each attention call over {min(args.steps, EVENT_STEPS)} decode "
                                "steps run right after the timed steps"},
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h["h2d_bytes_per_step"],
@@ -907,7 +918,8 @@ def run_ours(args):
             "ms_per_step": bf_elapsed / args.steps,
             "kv_gbs_per_gpu": bf["kv_bytes_step"] / (bf["elapsed_ms"] / args.steps * 1e-3) / 1e9,
             "roofline": {"achieved": bf_achieved, "peak": peak, "frac": bf_achieved / peak,
-                         "avg_launch_ms": bf["avg_launch_ms"], "bytes_per_launch": bf["bytes_per_launch"]},
+                         "avg_launch_ms": bf["avg_launch_ms"], "bytes_per_launch": bf["bytes_per_launch"],
+                         "traffic": DRAM_PER_ALGORITHMIC["bf16"] * bf["bytes_per_launch"]},
             "e2e_tok_s": bf_tokens / (bf_e2e_ms * 1e-3)},
             "cfg3_prefix_prefill": None if cfg3 is None else {
                 "workload": "256 seqs fork a 2050-token prefix (COW of the 2-token tail), suffix U[64,512] seed 2, "
