@@ -96,7 +96,6 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
     *out = nullptr;
     cudaStream_t stream = (cudaStream_t)stream_;
     S1KV_ON_DEVICE(p->device);
-    const int32_t bs = p->desc.block_size;
 
     auto* b = new s1kv_batch();
     b->pool = p;
