@@ -40,11 +40,16 @@ int check_layer(const s1kv_pool* p, int32_t layer) {
 }
 
 // Split-K plan: tiles of 16 tokens; the split length (in tiles) targets
-// about 8 waves of CTAs over the 148 SMs, at least one tile per warp and
-// at most 32 per warp (the kernel prefetches 32 block ids per warp).
-int32_t plan_split_tiles(int64_t total_tiles, int32_t Hkv, int nw) {
+// about 8 waves of CTAs over the 148 SMs, at least one tile per warp, and
+// no more than kMaxSplitsPerRow splits of the longest row (one CTA merges a
+// row's partials, so a row cut into hundreds of splits ends the launch with
+// a long merge), and at most 32 tiles per warp (the kernel prefetches 32
+// block ids per warp).
+constexpr int64_t kMaxSplitsPerRow = 64;
+int32_t plan_split_tiles(int64_t total_tiles, int64_t max_row_tiles, int32_t Hkv, int nw) {
     int64_t target = (int64_t)kSMs * 8;
     int64_t s = (total_tiles * Hkv + target - 1) / target;
+    s = std::max<int64_t>(s, (max_row_tiles + kMaxSplitsPerRow - 1) / kMaxSplitsPerRow);
     s = std::max<int64_t>(s, nw);
     s = std::min<int64_t>(s, 32 * nw);
     return (int32_t)s;
@@ -57,9 +62,12 @@ float scale_log2(int D) { return 1.4426950408889634f / std::sqrt((float)D); }
 void plan_items(const s1kv_pool* p, s1kv_batch* b) {
     const int32_t bs = p->desc.block_size;
     const int nw = tma_warps_per_cta(p->desc.dtype, p->desc.head_dim);
-    int64_t total_tiles = 0;
-    for (const RowMeta& m : b->rows) total_tiles += (m.kv_len + bs - 1) / bs;
-    b->split_tokens = plan_split_tiles(total_tiles, p->desc.num_kv_heads, nw) * 16;
+    int64_t total_tiles = 0, max_row_tiles = 0;
+    for (const RowMeta& m : b->rows) {
+        total_tiles += (m.kv_len + bs - 1) / bs;
+        max_row_tiles = std::max<int64_t>(max_row_tiles, (m.kv_len + bs - 1) / bs);
+    }
+    b->split_tokens = plan_split_tiles(total_tiles, max_row_tiles, p->desc.num_kv_heads, nw) * 16;
     std::vector<WorkItem>& items = b->items;
     items.clear();
     int64_t n_part = 0;

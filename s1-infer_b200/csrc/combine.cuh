@@ -64,7 +64,7 @@ __device__ __forceinline__ void combine_partials(const AttnParams& p, int row, i
 // The same merge with the splits' (max, sum) staged in shared memory
 // (`sm`, at least 2 * (n_split + 1) * G floats): the maxima, weights and
 // normaliser are computed in parallel, then every (head, dim) output sums
-// its n_split partials with eight loads in flight.  Long rows (cfg4: 64+
+// its n_split partials with eight splits' loads in flight.  Long rows (64+
 // splits per row) make the serial loop above latency-bound.
 __device__ __forceinline__ void combine_partials_staged(const AttnParams& p, int row, int h, int G, int D, float* sm) {
     const RowMeta rm = p.rows[row];
@@ -98,19 +98,62 @@ __device__ __forceinline__ void combine_partials_staged(const AttnParams& p, int
         mg[tid] = 1.0f / L;
     }
     __syncthreads();
-    for (int idx = tid; idx < G * D; idx += nt) {
-        const int g = idx / D, d = idx % D;
-        const float* po = p.part_o + ((int64_t)rm.part_off * p.Hkv + h) * G * D + g * D + d;
-        const int64_t stride = (int64_t)p.Hkv * G * D;  // next split, same head
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (D % 4 != 0) {
+        for (int idx = tid; idx < G * D; idx += nt) {
+            const int g = idx / D, d = idx % D;
+            const float* po = p.part_o + ((int64_t)rm.part_off * p.Hkv + h) * G * D + g * D + d;
+            const int64_t stride = (int64_t)p.Hkv * G * D;  // next split, same head
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            int s = 0;
+            for (; s + 8 <= ns; s += 8) {
+#pragma unroll
+                for (int u = 0; u < 8; u++) acc[u] = fmaf(__ldcg(po + (s + u) * stride), w[(s + u) * G + g], acc[u]);
+            }
+            for (; s < ns; s++) acc[0] = fmaf(__ldcg(po + s * stride), w[s * G + g], acc[0]);
+            const float O = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+            store_out(p, row, h * G + g, d, D, O * mg[g]);
+        }
+        return;
+    }
+    // Each thread sums 4 adjacent dims of one head (16-byte loads, eight
+    // splits in flight): per element the same sums in the same order as the
+    // scalar loop above, with 4x the bytes in flight.  A row's partials are
+    // ns * G * D * 4 bytes (1.2 MB at 293 splits of 8 heads), read by this one
+    // CTA, so its loads in flight set the merge time.
+    const float4* base = reinterpret_cast<const float4*>(p.part_o + ((int64_t)rm.part_off * p.Hkv + h) * G * D);
+    const int64_t stride4 = (int64_t)p.Hkv * G * D / 4;  // next split, same head
+    for (int c = tid; c < G * D / 4; c += nt) {
+        const int g = (4 * c) / D, d = (4 * c) % D;
+        const float4* po = base + c;
+        float4 acc[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         int s = 0;
         for (; s + 8 <= ns; s += 8) {
+            float4 v[8];
 #pragma unroll
-            for (int u = 0; u < 8; u++) acc[u] = fmaf(__ldcg(po + (s + u) * stride), w[(s + u) * G + g], acc[u]);
+            for (int u = 0; u < 8; u++) v[u] = __ldcg(po + (s + u) * stride4);
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const float f = w[(s + u) * G + g];
+                acc[u] = make_float4(fmaf(v[u].x, f, acc[u].x), fmaf(v[u].y, f, acc[u].y), fmaf(v[u].z, f, acc[u].z),
+                                     fmaf(v[u].w, f, acc[u].w));
+            }
         }
-        for (; s < ns; s++) acc[0] = fmaf(__ldcg(po + s * stride), w[s * G + g], acc[0]);
-        const float O = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
-        store_out(p, row, h * G + g, d, D, O * mg[g]);
+        for (; s < ns; s++) {
+            const float4 v = __ldcg(po + s * stride4);
+            const float f = w[s * G + g];
+            acc[0] = make_float4(fmaf(v.x, f, acc[0].x), fmaf(v.y, f, acc[0].y), fmaf(v.z, f, acc[0].z),
+                                 fmaf(v.w, f, acc[0].w));
+        }
+        const float r = mg[g];
+        const float o[4] = {
+            (((acc[0].x + acc[1].x) + (acc[2].x + acc[3].x)) + ((acc[4].x + acc[5].x) + (acc[6].x + acc[7].x))) * r,
+            (((acc[0].y + acc[1].y) + (acc[2].y + acc[3].y)) + ((acc[4].y + acc[5].y) + (acc[6].y + acc[7].y))) * r,
+            (((acc[0].z + acc[1].z) + (acc[2].z + acc[3].z)) + ((acc[4].z + acc[5].z) + (acc[6].z + acc[7].z))) * r,
+            (((acc[0].w + acc[1].w) + (acc[2].w + acc[3].w)) + ((acc[4].w + acc[5].w) + (acc[6].w + acc[7].w))) * r};
+#pragma unroll
+        for (int j = 0; j < 4; j++) store_out(p, row, h * G + g, d + j, D, o[j]);
     }
 }
 

@@ -246,6 +246,42 @@ def test_batched_decode_vs_oracle(s1kv, oracle, cuda, dtype, shape):
     assert pool.check_device() == 0
 
 
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_long_rows_capped_splits_vs_oracle(s1kv, oracle, cuda, dtype):
+    """Rows long enough for the split planner's cap of 64 splits per row
+    (one KV head, 8 query heads; 40,000 tokens = 2,500 tiles -> splits of 40
+    tiles, 63 of them): the last-arriving CTA of the row merges its 63
+    partials (16-byte loads, eight splits in flight). Each row against the
+    oracle's contiguous GQA attention, 2e-5 x max |ref| (bf16: on the
+    bf16-rounded K/V)."""
+    import torch
+    Hq, Hkv, D, bs = 8, 1, 128, 16
+    ctx = [40000, 9000, 300]
+    B = len(ctx)
+    rng = np.random.default_rng(31)
+    k = [rng.standard_normal((c, Hkv, D), dtype=np.float32) for c in ctx]
+    v = [rng.standard_normal((c, Hkv, D), dtype=np.float32) for c in ctx]
+    q = rng.standard_normal((B, Hq, D), dtype=np.float32)
+    need = sum((c + bs - 1) // bs for c in ctx)
+    pool = s1kv.Pool(1, Hkv, D, need + 4, bs, dtype=dtype,
+                     initial_free_list=np.random.default_rng(5).permutation(need + 4))
+    seqs = list(range(B))
+    with pool.batch(seqs, ctx, [0] * B) as b:
+        b.append(0, torch.from_numpy(np.concatenate(k)).cuda(), torch.from_numpy(np.concatenate(v)).cuda())
+    with pool.batch(seqs, [0] * B, [1] * B) as b:
+        split_tokens, _ = b.plan()
+        out = host(b.attention(0, torch.from_numpy(q).cuda()))
+    assert split_tokens == 40 * 16
+    assert (ctx[0] + split_tokens - 1) // split_tokens == 63
+    for s in range(B):
+        kk = oracle.bf16_round(k[s]) if dtype == "bf16" else k[s]
+        vv = oracle.bf16_round(v[s]) if dtype == "bf16" else v[s]
+        ref = oracle.gqa_attention(q[s:s + 1], kk, vv, Hq, Hkv, D)
+        assert rel_err(out[s:s + 1], ref) <= TOL_F32, (s, rel_err(out[s:s + 1], ref))
+    assert pool.check_device() == 0
+    pool.close()
+
+
 def test_bf16_storage_within_north_star_tolerance(s1kv, oracle, cuda):
     """bf16 K/V storage against the fp32 oracle (no rounding): 1e-2."""
     import torch
