@@ -76,7 +76,7 @@ void plan_items(const s1kv_pool* p, s1kv_batch* b) {
         m.n_split = (m.kv_len + b->split_tokens - 1) / b->split_tokens;
         m.part_off = (int32_t)n_part;
         if (m.n_split > 1) n_part += m.n_split;
-        for (int32_t s = 0; s < m.n_split; s++) items.push_back({(int32_t)r, s});
+        for (int32_t s = 0; s < m.n_split; s++) items.push_back({(int32_t)r, s, m.table_row, m.kv_len});
     }
     // Longest work first: full splits, then the tails by length.
     auto item_tokens = [&](const WorkItem& w) {

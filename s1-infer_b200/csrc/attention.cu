@@ -248,12 +248,11 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, 
     // and read the same token rows of the pool together
     const int h = (int)(blockIdx.x % (unsigned)p.Hkv);
     const WorkItem item = p.items[blockIdx.x / (unsigned)p.Hkv];
-    const RowMeta rm = p.rows[item.row];
     const int tok0 = item.split * p.split_tokens;
-    const int tok1 = min(tok0 + p.split_tokens, rm.kv_len);
+    const int tok1 = min(tok0 + p.split_tokens, item.kv_len);
     const int n_tiles = (tok1 - tok0 + TILE - 1) / TILE;
     const int my_tiles = n_tiles > warp ? (n_tiles - warp + NW - 1) / NW : 0;
-    const int32_t* tab = p.table + (int64_t)rm.table_row * p.max_bps;
+    const int32_t* tab = p.table + (int64_t)item.table_row * p.max_bps;
 
     uint8_t* ring = smem + warp * NS * C::kStageBytes;
     float* Ps = reinterpret_cast<float*>(smem + C::kRing) + warp * C::kPFloats;  // [TILE][NV]
@@ -293,6 +292,7 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, 
             if (lane == 0) issue(k, row);
         }
     }
+    const RowMeta rm = p.rows[item.row];  // split count and partial offset, needed at the end
 
     // q of the group's heads (padded heads are zero): lane part pp holds
     // chunks pp, pp+LPT, ... of each head as float pairs.

@@ -149,12 +149,11 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
     // heads-fastest order of the fp32 kernel measured 3% slower here)
     const int h = blockIdx.y;
     const WorkItem item = p.items[blockIdx.x];
-    const RowMeta rm = p.rows[item.row];
     const int tok0 = item.split * p.split_tokens;
-    const int tok1 = min(tok0 + p.split_tokens, rm.kv_len);
+    const int tok1 = min(tok0 + p.split_tokens, item.kv_len);
     const int n_tiles = (tok1 - tok0 + kTile - 1) / kTile;
     const int my_tiles = n_tiles > warp ? (n_tiles - warp + kNW - 1) / kNW : 0;
-    const int32_t* tab = p.table + (int64_t)rm.table_row * p.max_bps;
+    const int32_t* tab = p.table + (int64_t)item.table_row * p.max_bps;
     uint8_t* ring = smem + warp * kNS * kStageBytes;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kRing) + warp * kNS;
 
@@ -189,6 +188,7 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
         const int row = __shfl_sync(kFull, my_row, k);
         if (lane == 0) issue(k, row);
     }
+    const RowMeta rm = p.rows[item.row];  // split count and partial offset, needed at the end
 
     // B fragments of q^T (pre-scaled, split hi + lo): k-step ks covers dims
     // 16ks .. 16ks+15; this lane holds dims 2tq, 2tq+1 (b0) and 2tq+8, 2tq+9

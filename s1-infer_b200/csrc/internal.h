@@ -111,10 +111,14 @@ struct RowMeta {
     int32_t part_off;
 };
 
-// One split-K work item: query row and split index.
+// One split-K work item: query row and split index, with the row's block
+// table row and context length copied in, so a decode CTA can address its
+// first K/V tiles without first loading the row's RowMeta.
 struct WorkItem {
     int32_t row;
     int32_t split;
+    int32_t table_row;
+    int32_t kv_len;
 };
 
 struct AttnParams {

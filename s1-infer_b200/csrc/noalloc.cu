@@ -60,7 +60,7 @@ __global__ void noalloc_plan_kernel(const int32_t* __restrict__ seq_lens, int32_
         const int32_t n_split = (len + split_tokens - 1) / split_tokens;
         if (is_item) {
             const int32_t j = (int32_t)(i % max_splits);
-            items[i] = j < n_split ? WorkItem{s, j} : WorkItem{n_seqs, 0};
+            items[i] = j < n_split ? WorkItem{s, j, s, len} : WorkItem{n_seqs, 0, 0, 0};
         } else {
             rows[s] = RowMeta{s, len, n_split, s * max_splits};
         }
