@@ -41,11 +41,11 @@ EVENT_STEPS = 5  # decode steps of the per-launch timing pass that follows the t
 # DRAM bytes (read + write) per decode launch over its algorithmic bytes, from
 # one ncu capture of each kernel on the one- or two-layer case of this
 # workload (same shapes, 1.08 GB / 0.54 GB per launch, above L2):
-#   fp32 decode_tma_kernel: 1.081969 GB read + 5.774 MB written, 1.082991 GB algorithmic
-#   bf16 decode_mma_kernel: 0.542480 GB read + 7.267 MB written, 0.542561 GB algorithmic
+#   fp32 decode_tma_kernel: 1.082104 GB read + 6.259 MB written, 1.082991 GB algorithmic
+#   bf16 decode_mma_kernel: 0.542419 GB read + 6.341 MB written, 0.542561 GB algorithmic
 # Traffic grows with the context like the algorithmic bytes, so a launch of
 # the full run is reported as this ratio times its algorithmic bytes.
-DRAM_PER_ALGORITHMIC = {"f32": (1.081969e9 + 5.774e6) / 1.082991e9, "bf16": (0.542480e9 + 7.267e6) / 0.542561e9}
+DRAM_PER_ALGORITHMIC = {"f32": (1.082104e9 + 6.259e6) / 1.082991e9, "bf16": (0.542419e9 + 6.341e6) / 0.542561e9}
 SEQS_PER_GPU = 64
 CTX_LO, CTX_HI, CTX_SEED = 128, 4096, 1
 WORKLOAD = "cfg2: batched ragged paged decode, Llama-3-8B attention shape"
