@@ -282,7 +282,7 @@ def test_long_rows_capped_splits_vs_oracle(s1kv, oracle, cuda, dtype):
     pool.close()
 
 
-def test_bf16_storage_within_north_star_tolerance(s1kv, oracle, cuda):
+def test_bf16_storage_within_tolerance(s1kv, oracle, cuda):
     """bf16 K/V storage against the fp32 oracle (no rounding): 1e-2."""
     import torch
     rng = np.random.default_rng(77)
