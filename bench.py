@@ -599,7 +599,7 @@ def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3):
 
 
 def run_cfg5(s1kv, torch, rank, world, steps=100, warmup=20):
-    """cfg5, pool churn, one GPU's share of a sequence-sharded 8-GPU box
+    """cfg5, pool churn, one GPU's share of a sequence-sharded 8-GPU node
     (512 running sequences, 8 arrivals per step, 55k blocks per layer):
     64 running sequences on a pool of 6875 blocks per layer (32 layers,
     Hq 32 / Hkv 8 / D 128, bf16), Poisson(1) arrivals per step, prompts

@@ -1,7 +1,8 @@
 /*
  * kvoracle.c -- CPU oracle for the paged KV-cache path.  TEST INFRASTRUCTURE
  * ONLY: the parity tests, the smoke check and the bench's CPU-baseline leg
- * call it as the checker.  Nothing in the product library links or calls it.
+ * compare the library's results with it.  Nothing in the product library
+ * links or calls it.
  *
  * A plain-C restatement of liamma06/s1-infer's KV-cache hot path:
  *   - KVBlockPool bookkeeping and storage   src/infer/kv_block_pool.cpp:6-223

@@ -1,7 +1,8 @@
 """ctypes loader for the CPU oracle.  TEST INFRASTRUCTURE ONLY.
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
-this module, and only as the checker.  It exposes
+this module, and only to compare the library's results with it.  It
+exposes
 
   * ``Oracle``     -- the plain-C restatement (oracle/kvoracle.c), built by
                       oracle/Makefile from files in this repository;

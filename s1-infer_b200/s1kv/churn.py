@@ -24,7 +24,7 @@ import numpy as np
 
 
 class ChurnWorkload:
-    """Seeded request stream.  Defaults are one GPU's share of an 8-GPU box
+    """Seeded request stream.  Defaults are one GPU's share of an 8-GPU node
     serving 512 sequences with 8 arrivals per step: 64 running sequences,
     Poisson(1) arrivals per step; prompts log-normal (median 1024, sigma
     0.8, mean about 1410 tokens); outputs U[32, 512]; 30% of the prompts
