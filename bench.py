@@ -875,77 +875,77 @@ def run_ours(args):
     if rank != 0:
         return
     achieved = h["bytes_per_launch"] / (h["avg_launch_ms"] * 1e-3) / 1e9
-    tflops_peak, tflops_src = load_tflops_peak()
+    tflops_peak, _ = load_tflops_peak()
     bf_achieved = bf["bytes_per_launch"] / (bf["avg_launch_ms"] * 1e-3) / 1e9
+    step_s, bf_step_s = elapsed / args.steps * 1e-3, bf_elapsed / args.steps * 1e-3
+
+    def r(x, n=4):
+        return None if x is None else float(f"{x:.{n}g}")
+
+    # One compact line (numbers only; the workloads are described in DESIGN.md):
+    # every figure must survive in the few-KB tail of stdout the driver keeps.
     line = {
         "metric": METRIC,
-        "value": tokens / (elapsed * 1e-3),
+        "value": r(tokens / (elapsed * 1e-3), 6),
         "unit": "tok/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": elapsed / args.steps,
+        "ms_per_step": r(elapsed / args.steps, 5),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic (seeded normal Q/K/V, seeded context lengths and block permutation)",
-        "config": {"workload": WORKLOAD, "layers": LAYERS, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
-                   "block_size": BS, "seqs_per_gpu": SEQS_PER_GPU, "global_batch": SEQS_PER_GPU * world,
-                   "ctx": f"U[{CTX_LO},{CTX_HI}] seed {CTX_SEED}", "pool": "1.25x need, permuted",
-                   "kv_storage": "fp32", "parallelism": f"sequence-sharded x{world}, no collective",
-                   "l2": "inputs larger than L2 (1.1 GB of K/V per layer-step)"},
-        "kv_gbs_per_gpu": h["kv_bytes_step"] / (h["elapsed_ms"] / args.steps * 1e-3) / 1e9,
-        "hbm_frac_step": h["kv_bytes_step"] / (h["elapsed_ms"] / args.steps * 1e-3) / 1e9 / peak,
-        "roofline": {"bound": "hbm", "kernel": "paged split-K decode attention (decode + combine)",
-                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
-                     else "fallback 6650 GB/s", "bytes_per_launch": h["bytes_per_launch"],
-                     "avg_launch_ms": h["avg_launch_ms"],
-                     "traffic": DRAM_PER_ALGORITHMIC["f32"] * h["bytes_per_launch"],
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a one-layer capture, "
-                                       "scaled to this launch by its algorithmic bytes",
-                     "timing": f"CUDA events around each attention call over {min(args.steps, EVENT_STEPS)} decode "
-                               "steps run right after the timed steps"},
-        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h["h2d_bytes_per_step"],
-                "d2h_bytes_per_step": h["d2h_bytes_per_step"],
-                "path": "s1kv_batch_layer_host (C ABI, pinned host buffers, copies in the timed region)"},
+        "data": "synthetic",
+        "config": {"workload": "cfg2 batched ragged paged decode", "layers": LAYERS, "hq": HQ, "hkv": HKV, "d": D,
+                   "bs": BS, "seqs_per_gpu": SEQS_PER_GPU, "global_batch": SEQS_PER_GPU * world,
+                   "ctx": f"U[{CTX_LO},{CTX_HI}] seed {CTX_SEED}", "kv": "fp32",
+                   "parallelism": f"seq-shard x{world}", "l2": "inputs > L2, no flush"},
+        "roofline": {"bound": "hbm", "achieved": r(achieved), "peak": peak, "unit": "GB/s",
+                     "frac": r(achieved / peak), "traffic": r(DRAM_PER_ALGORITHMIC["f32"] * h["bytes_per_launch"]),
+                     "peak_src": peak_kind, "launch_ms": r(h["avg_launch_ms"]), "bytes": r(h["bytes_per_launch"]),
+                     "step_frac": r(h["kv_bytes_step"] / (h["elapsed_ms"] / args.steps * 1e-3) / 1e9 / peak)},
+        "e2e": {"value": r(tokens / (e2e_ms * 1e-3), 6), "unit": "tok/s",
+                "h2d_bytes_per_step": h["h2d_bytes_per_step"], "d2h_bytes_per_step": h["d2h_bytes_per_step"]},
         "gpu_launches": h["launches"],
-        "host_issue_ms_per_step": h["host_issue_ms_per_step"],
-        "clocks": h["clocks"],
-        "variants": {"bf16_kv": {
-            "value": bf_tokens / (bf_elapsed * 1e-3), "unit": "tok/s",
-            "ms_per_step": bf_elapsed / args.steps,
-            "kv_gbs_per_gpu": bf["kv_bytes_step"] / (bf["elapsed_ms"] / args.steps * 1e-3) / 1e9,
-            "roofline": {"achieved": bf_achieved, "peak": peak, "frac": bf_achieved / peak,
-                         "avg_launch_ms": bf["avg_launch_ms"], "bytes_per_launch": bf["bytes_per_launch"],
-                         "traffic": DRAM_PER_ALGORITHMIC["bf16"] * bf["bytes_per_launch"]},
-            "e2e_tok_s": bf_tokens / (bf_e2e_ms * 1e-3)},
-            "cfg3_prefix_prefill": None if cfg3 is None else {
-                "workload": "256 seqs fork a 2050-token prefix (COW of the 2-token tail), suffix U[64,512] seed 2, "
-                            "bf16, per layer",
-                "prefill_tflops": cfg3["prefill_tflops"], "unit": "TFLOP/s",
-                "roofline": {"bound": "tensor", "achieved": cfg3["prefill_tflops"], "peak": tflops_peak,
-                             "frac": cfg3["prefill_tflops"] / tflops_peak, "unit": "TFLOP/s",
-                             "peak_source": tflops_src},
-                "prefill_attn_ms_per_layer": cfg3["prefill_attn_ms"], "prefill_flops_per_layer": cfg3["prefill_flops"],
-                "prefill_step_ms_per_layer": cfg3["prefill_step_ms"], "cow_copies": cfg3["cow_copies"],
-                "decode_ms_per_step_per_layer": cfg3["decode_ms_per_step"],
-                "norm_rope_append": {"tokens": cfg3["append_tokens"], "fused_ms": cfg3["norm_rope_append_ms"],
-                                     "fused_gbs": cfg3["norm_rope_append_gbs"],
-                                     "rope_append_only_ms": cfg3["rope_append_ms"]}},
-            "cfg4_head_sharded": None if cfg4 is None else {
-                **cfg4, "roofline": {"bound": "hbm", "achieved": cfg4["kv_gbs_per_gpu"], "peak": peak,
-                                     "frac": cfg4["kv_gbs_per_gpu"] / peak, "unit": "GB/s"}},
-            "cfg5_churn": cfg5,
-            "int8_projections": None if int8 is None else {
-                **int8, "roofline": {"bound": "hbm", "path": "M = 1, products sharing x grouped (113 launches)",
-                                     "achieved": int8["M1"]["grouped_frac_of_hbm"] * peak, "peak": peak,
-                                     "frac": int8["M1"]["grouped_frac_of_hbm"], "unit": "GB/s",
-                                     "per_matrix_frac": int8["M1"]["frac_of_hbm"],
-                                     "lm_head_alone_frac": int8["M1"]["lm_head_frac_of_hbm"]}}},
-        "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "host_issue_ms": r(h["host_issue_ms_per_step"], 3),
+        "clocks": {k: h["clocks"].get(k) for k in ("sm_mhz", "sm_max_mhz", "reasons", "samples")} if h["clocks"] else None,
+        "cpu_baseline": None if cpu is None else {k: (r(cpu[k]) if k == "value" else cpu[k])
+                                                  for k in ("value", "unit", "cores", "kind", "sample")},
+        "variants": {
+            "bf16": {"tok_s": r(bf_tokens / (bf_elapsed * 1e-3), 5), "e2e_tok_s": r(bf_tokens / (bf_e2e_ms * 1e-3), 5),
+                     "ms_per_step": r(bf_elapsed / args.steps), "frac": r(bf_achieved / peak),
+                     "step_frac": r(bf["kv_bytes_step"] / (bf["elapsed_ms"] / args.steps * 1e-3) / 1e9 / peak),
+                     "launch_ms": r(bf["avg_launch_ms"])},
+        },
     }
+    v = line["variants"]
+    if cfg3 is not None:
+        v["cfg3"] = {"prefill_tflops": r(cfg3["prefill_tflops"]), "frac": r(cfg3["prefill_tflops"] / tflops_peak),
+                     "prefill_ms": r(cfg3["prefill_attn_ms"]), "step_ms": r(cfg3["prefill_step_ms"]),
+                     "cow": cfg3["cow_copies"], "decode_ms": r(cfg3["decode_ms_per_step"]),
+                     "nra_ms": r(cfg3["norm_rope_append_ms"]), "nra_frac": r(cfg3["norm_rope_append_gbs"] / peak),
+                     "ra_ms": r(cfg3["rope_append_ms"])}
+    if cfg4 is not None:
+        v["cfg4"] = {"tok_s": r(cfg4["tok_s"]), "ms_per_step": r(cfg4["ms_per_step_80_layers"]),
+                     "layers_timed": cfg4["layers_timed"], "attn_ms": r(cfg4["attn_ms_per_layer"]),
+                     "frac": r(cfg4["kv_gbs_per_gpu"] / peak), "wait_ms": r(cfg4["exchange_wait_ms_per_layer"]),
+                     "nccl_tok_s": r(cfg4["nccl_allgather"]["tok_s"]), "scaling": "strong"}
+    if cfg5 is not None:
+        v["cfg5"] = {"decode_tok_s": r(cfg5["decode_tok_s"]), "ms_per_step": r(cfg5["ms_per_step"]),
+                     "gpu_ms": r(cfg5["gpu_ms_per_step"]), "host_ms": r(cfg5["host_bookkeeping_ms_per_step"]),
+                     "evictions": cfg5["evictions_total"]}
+    if int8 is not None:
+        m1, m8 = int8["M1"], int8["M8"]
+        v["int8"] = {"m1_ms": r(m1["grouped_ms_per_step"]), "m1_frac": r(m1["grouped_frac_of_hbm"]),
+                     "m1_launches": m1["grouped_launches_per_step"], "m1_ungrouped_frac": r(m1["frac_of_hbm"]),
+                     "lm_head_frac": r(m1["lm_head_frac_of_hbm"]), "m8_ms": r(m8["grouped_ms_per_step"]),
+                     "m8_frac": r(m8["grouped_frac_of_hbm"]), "m1_e2e_tok_s": r(m1["e2e_tok_s"]),
+                     "cpu_tok_s": r(int8["cpu_baseline"]["value"]) if "cpu_baseline" in int8 else None}
+    if args.detail:
+        with open(args.detail, "w") as f:
+            json.dump({"f32": h, "bf16": bf, "cfg3": cfg3, "cfg4": cfg4, "cfg5": cfg5, "int8": int8, "cpu": cpu}, f,
+                      indent=1, default=str)
     print(json.dumps(line))
 
 
@@ -983,16 +983,20 @@ def run_reference(args):
         one_layer()
     dt = (time.perf_counter() - t0) / args.steps
     tok_s = B / (LAYERS * dt)
+    # Each timed step is ONE of the 32 layers of a decode step (the bounded
+    # sample); the per-step figures below are that layer's time scaled x32
+    # and say so.
     line = {
         "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * LAYERS * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded normal Q/K/V, seeded context lengths)",
-        "config": {"workload": WORKLOAD, "layers": LAYERS, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
-                   "block_size": BS, "seqs_per_gpu": SEQS_PER_GPU, "global_batch": SEQS_PER_GPU * world,
-                   "ctx": f"U[{CTX_LO},{CTX_HI}] seed {CTX_SEED}", "kv_storage": "fp32",
-                   "parallelism": "host CPU, rank 0 only"},
-        "kv_gbs_per_gpu": decode_bytes([c + 1 for c in share], 4) / dt / 1e9,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * LAYERS * 1e3,
+        "ms_per_step_kind": f"extrapolated: measured layer ms x {LAYERS}",
+        "layers_timed": 1, "ms_per_layer_measured": dt * 1e3, "timed_region_s": dt * args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg2 batched ragged paged decode", "layers": LAYERS, "hq": HQ, "hkv": HKV, "d": D,
+                   "bs": BS, "seqs_per_gpu": SEQS_PER_GPU, "global_batch": B,
+                   "ctx": f"U[{CTX_LO},{CTX_HI}] seed {CTX_SEED}", "kv": "fp32",
+                   "parallelism": "host CPU, rank 0 only (the sequences of one GPU)"},
+        "kv_gbs": decode_bytes([c + 1 for c in share], 4) / dt / 1e9,
         "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": n_threads if kind == "reference" else 1,
                          "kind": kind,
                          "sample": f"each step = 1 of {LAYERS} layers x {B} sequences x 1 decode token "
@@ -1014,6 +1018,7 @@ def main():
                     help="profiling case: run one variant")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cfg3-seqs", type=int, default=256, help="profiling case: sequences of the cfg3 variant")
+    ap.add_argument("--detail", help="also write every figure of the run, unrounded, to this JSON file")
     args = ap.parse_args()
     globals()["LAYERS"] = args.layers
     if args.warmup < 3:

@@ -114,7 +114,9 @@ int s1kv_pool_storage(const s1kv_pool* pool, int32_t layer, void** k_base, void*
 int s1kv_pool_read(s1kv_pool* pool, int32_t layer, int32_t which, int64_t slot0, int64_t n_slots, void* host_out);
 
 /* s1kv_pool_check for the device error word of CUDA device `device`
- * (shared by every pool and call on that device). */
+ * (shared by every pool and call on that device), OR-ed with the error word
+ * of s1kv_decode_attention_noalloc's fixed array on that device; both are
+ * cleared.  Allocates nothing. */
 int s1kv_device_check(int device, int32_t* flags_out);
 
 /* Reads and clears the device error word (synchronises the device).  Bit 0:
@@ -302,12 +304,16 @@ int s1kv_attention(s1kv_pool* pool, int32_t layer, const uint64_t* seqs, const i
  * ceil(max_seq_len / split) x num_kv_heads x (n_q_heads / num_kv_heads) x
  * (head_dim + 2) x 4 bytes) returns S1KV_EINVAL with the sizes in
  * s1kv_last_error().  The first call on a device does a one-time set-up
- * (looks up the array's device address and clears its error word), so make
- * that first call before any stream capture.  Every call reuses the same
- * array, which keeps the last call's contents: calls that overlap on the
- * GPU (other streams, other host threads) race and must be serialised by
- * the caller.  Sequence lengths outside [1, max_seq_len] are recorded in the
- * array's error word and their output rows are unspecified. */
+ * (looks up the array's device address and clears its error word on
+ * `stream`), so make that first call before any stream capture.  Every
+ * call reuses the same array, which keeps the last call's contents: calls
+ * that overlap on the GPU (other streams, other host threads) race and must
+ * be serialised by the caller.  The set-up is cached per device ordinal for the life of the
+ * process: cudaDeviceReset after the first call is not supported.
+ * Sequence lengths outside [1, max_seq_len] (bit 0) and a timed-out copy
+ * wait (bit 1) set the array's error word, and the affected output rows are
+ * unspecified; s1kv_device_check(device) reads and clears that word, with
+ * no allocation. */
 int s1kv_decode_attention_noalloc(const void* k_cache, const void* v_cache, int32_t dtype, int64_t num_slots,
                                   int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
                                   const int32_t* block_tables, int32_t max_blocks_per_seq, const int32_t* seq_lens,

@@ -697,11 +697,18 @@ namespace s1kv {
 
 int encode_kv_maps(const void* k, const void* v, int dtype, int Hkv, int D, int64_t num_slots, CUtensorMap* tk,
                    CUtensorMap* tv) {
-    cudaDriverEntryPointQueryResult q;
-    void* fn = nullptr;
-    S1KV_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
-    if (q != cudaDriverEntryPointSuccess || !fn) return set_error(S1KV_ECUDA, "s1kv: cuTensorMapEncodeTiled unavailable");
-    auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    // the driver entry point is looked up once per process
+    static std::atomic<PFN_cuTensorMapEncodeTiled_v12000> cached{nullptr};
+    PFN_cuTensorMapEncodeTiled_v12000 encode = cached.load(std::memory_order_acquire);
+    if (!encode) {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        S1KV_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !fn)
+            return set_error(S1KV_ECUDA, "s1kv: cuTensorMapEncodeTiled unavailable");
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        cached.store(encode, std::memory_order_release);
+    }
     const cuuint64_t e = dtype == S1KV_DTYPE_F32 ? 4 : 2;
     const CUtensorMapDataType dt =
         dtype == S1KV_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -721,7 +728,13 @@ int encode_kv_maps(const void* k, const void* v, int dtype, int Hkv, int D, int6
 template <typename T, int D, int G>
 static int launch_with_maps_t(const AttnParams& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream) {
     using C = DecodeCfg<T, D, G>;
-    S1KV_CUDA(cudaFuncSetAttribute(decode_tma_kernel<T, D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+    static std::atomic<uint64_t> attr_set{0};  // per device
+    int st = once_per_device(attr_set, [] {
+        S1KV_CUDA(cudaFuncSetAttribute(decode_tma_kernel<T, D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::kSmem));
+        return S1KV_OK;
+    });
+    if (st) return st;
     if ((int64_t)p.n_items * p.Hkv > INT32_MAX) return set_error(S1KV_EINVAL, "decode: too many work items");
     decode_tma_kernel<T, D, G><<<dim3((unsigned)((int64_t)p.n_items * p.Hkv)), C::kNW * 32, C::kSmem, stream>>>(p, tk, tv);
     g_launches++;

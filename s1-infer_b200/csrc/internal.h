@@ -99,6 +99,9 @@ __device__ __forceinline__ void pdl_enter() {
 constexpr int kErrBounds = 1;
 constexpr int kErrTimeout = 2;
 int* device_error_word(int device);
+// Reads and clears the no-allocation decode's error word on `device`
+// (noalloc.cu); *flags = 0 if that entry point never ran there.
+int noalloc_take_error(int device, int* flags);
 
 // -------------------------------------------------------- device structs --
 // One query row of attention: its sequence's block-table row, the number

@@ -68,6 +68,27 @@ __global__ void noalloc_plan_kernel(const int32_t* __restrict__ seq_lens, int32_
 }
 
 }  // namespace
+
+// Reads and clears the error word of the array on `device` (the current
+// device), if a no-allocation call ever ran there: synchronous symbol
+// copies, no allocation.  *flags gets the word (0 when never set up).
+int noalloc_take_error(int device, int* flags) {
+    *flags = 0;
+    if (device < 0 || device >= kMaxDevices) return S1KV_OK;
+    {
+        std::lock_guard<std::mutex> g(g_mu);
+        if (!g_addr[device]) return S1KV_OK;
+    }
+    int h = 0;
+    S1KV_CUDA(cudaMemcpyFromSymbol(&h, g_noalloc_scratch, sizeof(int), 0, cudaMemcpyDeviceToHost));
+    if (h) {
+        const int zero = 0;
+        S1KV_CUDA(cudaMemcpyToSymbol(g_noalloc_scratch, &zero, sizeof(int), 0, cudaMemcpyHostToDevice));
+    }
+    *flags = h;
+    return S1KV_OK;
+}
+
 }  // namespace s1kv
 
 using namespace s1kv;
@@ -120,6 +141,9 @@ extern "C" int s1kv_decode_attention_noalloc(const void* k_cache, const void* v_
 
     // Set-up, once per device: the device address of the array.  In host
     // code g_noalloc_scratch names a host-side stand-in, not device memory.
+    // The error word is cleared on the caller's stream, ahead of this
+    // call's kernels (device globals also start at zero when the module
+    // loads).
     int dev = 0;
     S1KV_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kMaxDevices) return set_error(S1KV_EINVAL, "s1kv_decode_attention_noalloc: device id");
@@ -130,8 +154,8 @@ extern "C" int s1kv_decode_attention_noalloc(const void* k_cache, const void* v_
             void* p = nullptr;
             cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
             if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
-            e = cudaMemset(p, 0, 256);  // the error word starts at zero
-            if (e != cudaSuccess) return cuda_error(e, "cudaMemset(error word)");
+            e = cudaMemsetAsync(p, 0, 256, stream);
+            if (e != cudaSuccess) return cuda_error(e, "cudaMemsetAsync(error word)");
             g_addr[dev] = p;
         }
         base = (unsigned char*)g_addr[dev];

@@ -38,18 +38,29 @@ int cuda_error(cudaError_t e, const char* what) {
                      cudaGetErrorString(e));
 }
 
+namespace {
+std::mutex g_word_mu;
+std::unordered_map<int, int*> g_words;
+}  // namespace
+
 int* device_error_word(int device) {
-    static std::mutex mu;
-    static std::unordered_map<int, int*> words;
-    std::lock_guard<std::mutex> g(mu);
-    auto it = words.find(device);
-    if (it != words.end()) return it->second;
+    std::lock_guard<std::mutex> g(g_word_mu);
+    auto it = g_words.find(device);
+    if (it != g_words.end()) return it->second;
     int* p = nullptr;
     if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
     cudaMemset(p, 0, sizeof(int));
     cudaDeviceSynchronize();
-    words[device] = p;
+    g_words[device] = p;
     return p;
+}
+
+// The word of `device` if some call already created it, else NULL (no
+// allocation).
+static int* existing_error_word(int device) {
+    std::lock_guard<std::mutex> g(g_word_mu);
+    auto it = g_words.find(device);
+    return it == g_words.end() ? nullptr : it->second;
 }
 
 // ---------------------------------------------------------------- stager --
@@ -528,12 +539,19 @@ int s1kv_pool_check(s1kv_pool* p, int32_t* flags_out) {
 
 int s1kv_device_check(int device, int32_t* flags_out) {
     S1KV_ON_DEVICE(device);
-    int* word = device_error_word(device);
-    if (!word) return set_error(S1KV_ENOMEM, "s1kv: error word allocation failed");
     S1KV_CUDA(cudaDeviceSynchronize());
     int h = 0;
-    S1KV_CUDA(cudaMemcpy(&h, word, sizeof(int), cudaMemcpyDeviceToHost));
-    S1KV_CUDA(cudaMemset(word, 0, sizeof(int)));
+    // the word shared by pools and single calls (created by the first of
+    // them), then the no-allocation decode's own word in its fixed array;
+    // reading allocates nothing
+    if (int* word = existing_error_word(device)) {
+        S1KV_CUDA(cudaMemcpy(&h, word, sizeof(int), cudaMemcpyDeviceToHost));
+        if (h) S1KV_CUDA(cudaMemset(word, 0, sizeof(int)));
+    }
+    int na = 0;
+    const int st = noalloc_take_error(device, &na);
+    if (st) return st;
+    h |= na;
     if (flags_out) *flags_out = h;
     if (h & kErrTimeout) return set_error(S1KV_ETIMEOUT, "s1kv: a bounded device wait timed out");
     if (h & kErrBounds) return set_error(S1KV_EDEVICE, "s1kv: a kernel saw an out-of-range slot or block");

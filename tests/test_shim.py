@@ -52,12 +52,26 @@ def test_shim_program_on_gpu():
     assert "0 failed" in r.stdout
 
 
+def test_reference_unit_tests_build_against_shim():
+    """`make -C oracle shimtests` compiles the reference's unit tests
+    unchanged against the shim wherever the reference sources are present;
+    the binaries must then exist (build outputs, never committed)."""
+    if not os.path.exists(SHIM_LIB):
+        subprocess.run(["python", os.path.join(ROOT, "s1-infer_b200", "build.py")], check=True)
+    r = subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "shimtests"], capture_output=True,
+                       text=True, check=True)
+    if "skipping shimtests" in r.stdout:
+        pytest.skip("reference sources absent on this machine; the binaries travel prebuilt")
+    for name in ("test_kv_block_pool", "test_attention", "test_rope"):
+        assert os.path.exists(os.path.join(REF_DIR, f"{name}_on_shim")), name
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", ["test_kv_block_pool", "test_attention", "test_rope"])
 def test_reference_unit_tests_on_shim(name):
     exe = os.path.join(REF_DIR, f"{name}_on_shim")
-    if not os.path.exists(exe):
-        pytest.skip("the reference's tests were not compiled against the shim here (oracle/_ref)")
+    assert os.path.exists(exe), ("the reference's tests compiled against the shim are missing: run "
+                                 "`make -C oracle shimtests` where the reference sources are present")
     r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "Status: SUCCESS" in r.stdout, r.stdout
