@@ -226,6 +226,13 @@ typedef struct s1kv_exchange s1kv_exchange;
 int s1kv_exchange_create(int device, int32_t rank, int32_t world, int64_t slot_floats, s1kv_exchange** out);
 int s1kv_exchange_handle(const s1kv_exchange* ex, void* handle64);
 int s1kv_exchange_open(s1kv_exchange* ex, const void* handles);
+/* For ranks that live in ONE process (one host thread per GPU, or several
+ * ranks' exchanges on one GPU): bases[world] holds every rank's
+ * s1kv_exchange_base() in rank order, device memory that this exchange's
+ * GPU can reach (the same GPU, or a peer GPU: peer access is enabled here).
+ * Replaces the IPC handle exchange of s1kv_exchange_open. */
+void* s1kv_exchange_base(const s1kv_exchange* ex);
+int s1kv_exchange_open_local(s1kv_exchange* ex, void* const* bases);
 /* Device address of the slot `epoch` uses: [rows][heads_total][head_dim]. */
 float* s1kv_exchange_buffer(const s1kv_exchange* ex, uint32_t epoch);
 int s1kv_exchange_wait(s1kv_exchange* ex, uint32_t epoch, void* stream);

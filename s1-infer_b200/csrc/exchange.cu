@@ -109,6 +109,38 @@ int s1kv_exchange_open(s1kv_exchange* ex, const void* handles) {
         void* ptr = nullptr;
         S1KV_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
         ex->peer_base[q] = static_cast<char*>(ptr);
+        ex->peer_ipc[q] = true;
+    }
+    ex->opened = true;
+    return S1KV_OK;
+}
+
+void* s1kv_exchange_base(const s1kv_exchange* ex) { return ex ? ex->base : nullptr; }
+
+int s1kv_exchange_open_local(s1kv_exchange* ex, void* const* bases) {
+    if (!ex || !bases) return set_error(S1KV_EINVAL, "null argument");
+    S1KV_ON_DEVICE(ex->device);
+    for (int q = 0; q < ex->world; q++) {
+        if (q == ex->rank || ex->peer_base[q]) continue;
+        if (!bases[q]) return set_error(S1KV_EINVAL, "s1kv_exchange_open_local: null base of rank %d", q);
+        cudaPointerAttributes a{};
+        S1KV_CUDA(cudaPointerGetAttributes(&a, bases[q]));
+        if (a.type != cudaMemoryTypeDevice)
+            return set_error(S1KV_EINVAL, "s1kv_exchange_open_local: base of rank %d is not device memory", q);
+        if (a.device != ex->device) {
+            // another GPU of this process: its memory must be reachable by
+            // peer access from this one
+            int can = 0;
+            S1KV_CUDA(cudaDeviceCanAccessPeer(&can, ex->device, a.device));
+            if (!can)
+                return set_error(S1KV_EINVAL, "s1kv_exchange_open_local: device %d cannot reach device %d",
+                                 ex->device, a.device);
+            const cudaError_t e = cudaDeviceEnablePeerAccess(a.device, 0);
+            if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+            else if (e != cudaSuccess) return cuda_error(e, "cudaDeviceEnablePeerAccess");
+        }
+        ex->peer_base[q] = static_cast<char*>(bases[q]);
+        ex->peer_ipc[q] = false;
     }
     ex->opened = true;
     return S1KV_OK;
@@ -134,7 +166,7 @@ int s1kv_exchange_destroy(s1kv_exchange* ex) {
     DeviceGuard guard(ex->device);
     cudaDeviceSynchronize();
     for (int q = 0; q < ex->world; q++)
-        if (ex->peer_base[q]) cudaIpcCloseMemHandle(ex->peer_base[q]);
+        if (ex->peer_base[q] && ex->peer_ipc[q]) cudaIpcCloseMemHandle(ex->peer_base[q]);
     if (ex->base) cudaFree(ex->base);
     delete ex;
     return S1KV_OK;

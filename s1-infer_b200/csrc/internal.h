@@ -321,7 +321,8 @@ struct s1kv_exchange {
     int device = 0, rank = 0, world = 1;
     int64_t slot_floats = 0;          // one layer's gathered output [B][Hq_total][D]
     char* base = nullptr;             // [2 slots][slot_floats] floats, then flags[2][8], then done counter
-    char* peer_base[8] = {};          // other ranks' bases (IPC), NULL for self
+    char* peer_base[8] = {};          // other ranks' bases, NULL for self
+    bool peer_ipc[8] = {};            // opened from a CUDA IPC handle (closed on destroy)
     bool opened = false;
     int* d_err = nullptr;
 };

@@ -113,6 +113,8 @@ SIGNATURES = {
     "s1kv_exchange_create": (C.c_int, [C.c_int, i32, i32, i64, P(vp)]),
     "s1kv_exchange_handle": (C.c_int, [vp, vp]),
     "s1kv_exchange_open": (C.c_int, [vp, vp]),
+    "s1kv_exchange_base": (vp, [vp]),
+    "s1kv_exchange_open_local": (C.c_int, [vp, vp]),
     "s1kv_exchange_buffer": (vp, [vp, C.c_uint32]),
     "s1kv_exchange_wait": (C.c_int, [vp, C.c_uint32, vp]),
     "s1kv_exchange_destroy": (C.c_int, [vp]),
@@ -665,7 +667,7 @@ class PeerExchange:
     epoch; wait(epoch) makes the stream wait (bounded) for all ranks.  The
     CUDA IPC handles are exchanged once through torch.distributed."""
 
-    def __init__(self, rank, world, rows, heads_total, head_dim, device=None, group=None):
+    def __init__(self, rank, world, rows, heads_total, head_dim, device=None, group=None, local=False):
         import torch
         self.L = lib()
         self.rank, self.world = rank, world
@@ -674,7 +676,7 @@ class PeerExchange:
         h = vp()
         check(self.L.s1kv_exchange_create(dev, rank, world, rows * heads_total * head_dim, C.byref(h)))
         self.h = h
-        if world > 1:
+        if world > 1 and not local:
             import torch.distributed as dist
             mine = (C.c_char * 64)()
             check(self.L.s1kv_exchange_handle(h, mine))
@@ -682,6 +684,16 @@ class PeerExchange:
             dist.all_gather_object(handles, bytes(mine), group=group)
             arr = (C.c_char * (64 * world)).from_buffer_copy(b"".join(handles))
             check(self.L.s1kv_exchange_open(h, arr))
+
+    @staticmethod
+    def open_local(exchanges):
+        """Opens the exchanges of all ranks of one process (created with
+        local=True, in rank order) on each other's device memory instead of
+        CUDA IPC handles (s1kv_exchange_open_local)."""
+        L = lib()
+        bases = (vp * len(exchanges))(*[L.s1kv_exchange_base(e.h) for e in exchanges])
+        for e in exchanges:
+            check(L.s1kv_exchange_open_local(e.h, bases))
 
     def attention(self, batch, layer, q, head0, epoch):
         """Decode attention of this rank's query heads q [rows, Hq_local, D]

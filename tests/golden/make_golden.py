@@ -14,6 +14,11 @@ Writes:
   <scenario>.npz  paged-attention outputs and block tables of the scenarios
                   in scenarios.py (prefill + decode through KVBlockPool,
                   apply_rope, GQA_attention_paged)
+  cfg1_full.npz   the same for the full cfg1 workload (24 layers, prefill
+                  512, 64 decode steps): SHA-256 of every output, a few
+                  outputs as values, the block table
+
+    python tests/golden/make_golden.py [--only-full]
 """
 from __future__ import annotations
 
@@ -137,16 +142,37 @@ def make_int8():
     np.savez_compressed(os.path.join(HERE, "int8.npz"), **out)
 
 
+def make_full(name):
+    """A BASELINE-sized scenario (scenarios.FULL_SCENARIOS): the SHA-256 of
+    every attention output of the reference (pins the oracle bit for bit at
+    full size), a few outputs as values, and the block tables."""
+    res = S.run_scenario(name, RefBackend())
+    outs = S.outputs(res, name)
+    keys = S.output_keys(name)
+    fx = {"keys": np.array(keys), "sha256": np.stack([np.frombuffer(S.digest(outs[k]), np.uint8) for k in keys])}
+    for key, prefill in S.kept_values(name):
+        fx["value/" + key] = outs[key][-S.PREFILL_ROWS_KEPT:] if prefill else outs[key]
+    for seq, t in res["tables"].items():
+        fx[f"table_s{seq}"] = t
+    np.savez_compressed(os.path.join(HERE, f"{name}_full.npz"), **fx)
+
+
 def main():
     O.build()
     if not O.ref_available():
         sys.exit("oracle/_ref/libs1ref.so missing: the reference sources are needed to make fixtures")
+    if "--only-full" in sys.argv:
+        for name in S.FULL_SCENARIOS:
+            make_full(name)
+        return
     make_rope()
     make_pool_ops()
     make_int8()
     for name in S.SCENARIOS:
         res = S.run_scenario(name, RefBackend())
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **S.flatten(res, name))
+    for name in S.FULL_SCENARIOS:
+        make_full(name)
     print("fixtures written to", HERE)
 
 

@@ -46,6 +46,20 @@ SCENARIOS = {
 }
 
 
+# BASELINE-sized scenario, pinned by digests (the reference's outputs are
+# too large to commit in full): cfg1 exactly -- 24 layers, Hq14/Hkv2/D64,
+# RoPE theta 1e6, fp32, block 16, seed 0, free list shuffled (the remove
+# trick), prefill 512 tokens then 64 decode steps.  48 physical blocks
+# hold the 576 tokens (36 blocks) with room to scatter.
+FULL_SCENARIOS = {
+    "cfg1": dict(layers=24, Hq=14, Hkv=2, D=64, bs=16, max_blocks=48, seed=0, seqs=[0], prefill=[512], steps=64),
+}
+
+
+def spec(name):
+    return SCENARIOS[name] if name in SCENARIOS else FULL_SCENARIOS[name]
+
+
 def run_scenario(name, backend):
     """Runs a scenario through `backend` and returns its outputs:
     {"out": [layer][step][seq] -> [1, Hq, D], "tables": {seq: [...]},
@@ -54,7 +68,7 @@ def run_scenario(name, backend):
     backend(pool_args) must provide: new_pools(layers, H, D, max_blocks, bs,
     free_order), rope(x, start_pos), append(layer, seq, k, v),
     attention(layer, seq, q, Hq), length(seq), table(seq)."""
-    s = SCENARIOS[name]
+    s = spec(name)
     rng = np.random.default_rng(s["seed"])
     order = rng.permutation(s["max_blocks"]).astype(np.int32)
     backend.new_pools(s["layers"], s["Hkv"], s["D"], s["max_blocks"], s["bs"], order)
@@ -89,7 +103,7 @@ def scenario_inputs(name):
     """Regenerates every input of a scenario in the order run_scenario
     draws them: (order, prefill[(layer, seq)] -> (q, k, v),
     decode[(step, seq, layer)] -> (q, k, v))."""
-    s = SCENARIOS[name]
+    s = spec(name)
     rng = np.random.default_rng(s["seed"])
     order = rng.permutation(s["max_blocks"]).astype(np.int32)
     L, Hq, Hkv, D = s["layers"], s["Hq"], s["Hkv"], s["D"]
@@ -110,7 +124,7 @@ PREFILL_ROWS_KEPT = 4
 def flatten(res, name):
     """Scenario result -> flat dict of arrays for np.savez (the last
     PREFILL_ROWS_KEPT query rows of each prefill, every decode output)."""
-    s = SCENARIOS[name]
+    s = spec(name)
     out = {}
     for layer in range(s["layers"]):
         for si, seq in enumerate(s["seqs"]):
@@ -120,6 +134,47 @@ def flatten(res, name):
     for seq, t in res["tables"].items():
         out[f"table_s{seq}"] = t
     return out
+
+
+def output_keys(name):
+    """Keys of every attention output of a scenario: the whole prefill
+    output of each (layer, sequence) and each decode output."""
+    s = spec(name)
+    keys = []
+    for layer in range(s["layers"]):
+        for seq in s["seqs"]:
+            keys.append(f"prefill_l{layer}_s{seq}")
+            keys += [f"dec_l{layer}_t{t}_s{seq}" for t in range(s["steps"])]
+    return keys
+
+
+def outputs(res, name):
+    """Scenario result -> {output key: array} (every output, full size)."""
+    s = spec(name)
+    out = {}
+    for layer in range(s["layers"]):
+        for si, seq in enumerate(s["seqs"]):
+            out[f"prefill_l{layer}_s{seq}"] = res["prefill_out"][layer][si]
+            for t in range(s["steps"]):
+                out[f"dec_l{layer}_t{t}_s{seq}"] = res["out"][layer][t][si]
+    return out
+
+
+def digest(a):
+    """SHA-256 of an output's fp32 bytes (C order): bit-exact identity."""
+    import hashlib
+    return hashlib.sha256(np.ascontiguousarray(a, dtype=np.float32).tobytes()).digest()
+
+
+# Outputs a full-size fixture keeps as values (besides every digest): the
+# first and last layer at the first, middle and last decode step, and the
+# last PREFILL_ROWS_KEPT prefill rows of those layers.
+def kept_values(name):
+    s = spec(name)
+    layers = sorted({0, s["layers"] - 1})
+    steps = sorted({0, s["steps"] // 2, s["steps"] - 1})
+    return [(f"prefill_l{l}_s{q}", True) for l in layers for q in s["seqs"]] + \
+           [(f"dec_l{l}_t{t}_s{q}", False) for l in layers for t in steps for q in s["seqs"]]
 
 
 # ---------------------------------------------------------------- pool ops --

@@ -326,3 +326,19 @@ def test_restatement_matches_reference_rmsnorm(oracle, D):
     x = rng.standard_normal((37, 5, D), dtype=np.float32) * 3
     w = rng.standard_normal(D, dtype=np.float32)
     assert np.array_equal(bits(oracle.rmsnorm(x, w)), bits(oracle.ref_rmsnorm(x, w)))
+
+
+@pytest.mark.parametrize("name", list(S.FULL_SCENARIOS))
+def test_full_scenario_digests_bit_exact(oracle, name):
+    """The oracle at BASELINE size (cfg1: 24 layers, prefill 512, 64 decode
+    steps): every attention output's SHA-256 equals the reference's, so the
+    oracle the GPU tests compare against is pinned bit for bit at full size."""
+    g = np.load(os.path.join(GOLDEN, f"{name}_full.npz"))
+    res = S.run_scenario(name, OracleBackend())
+    outs = S.outputs(res, name)
+    keys = [str(k) for k in g["keys"]]
+    assert keys == S.output_keys(name)
+    bad = [k for k, h in zip(keys, g["sha256"]) if S.digest(outs[k]) != h.tobytes()]
+    assert not bad, bad[:5]
+    for seq, t in res["tables"].items():
+        np.testing.assert_array_equal(t, g[f"table_s{seq}"])
