@@ -40,18 +40,17 @@ int check_layer(const s1kv_pool* p, int32_t layer) {
 }
 
 // Split-K plan: tiles of 16 tokens; the split length (in tiles) targets
-// about 8 waves of CTAs over the 148 SMs, at least one tile per warp, and
-// no more than kMaxSplitsPerRow splits of the longest row (one CTA merges a
-// row's partials, so a row cut into hundreds of splits ends the launch with
-// a long merge), and at most 32 tiles per warp (the kernel prefetches 32
-// block ids per warp).
-constexpr int64_t kMaxSplitsPerRow = 64;
+// about 8 waves of CTAs over the 148 SMs, at least one tile per warp, at
+// most 32 tiles per warp where the rows allow it (the kernels prefetch 32
+// block ids per warp and look further ones up as they go), and no more than
+// kMaxSplitsPerRow splits of the longest row (the merge's counters and
+// groups are sized for that).
 int32_t plan_split_tiles(int64_t total_tiles, int64_t max_row_tiles, int32_t Hkv, int nw) {
     int64_t target = (int64_t)kSMs * 8;
     int64_t s = (total_tiles * Hkv + target - 1) / target;
-    s = std::max<int64_t>(s, (max_row_tiles + kMaxSplitsPerRow - 1) / kMaxSplitsPerRow);
     s = std::max<int64_t>(s, nw);
     s = std::min<int64_t>(s, 32 * nw);
+    s = std::max<int64_t>(s, (max_row_tiles + kMaxSplitsPerRow - 1) / kMaxSplitsPerRow);
     return (int32_t)s;
 }
 
@@ -406,7 +405,7 @@ static int split_k_attention(s1kv_batch* b, int32_t layer, const float* q, float
     ap.layer = layer;
     ap.scale_log2 = scale_log2(D);
     ap.err = p->d_err;
-    const size_t cbytes = (size_t)b->n_rows * Hkv * sizeof(int32_t);
+    const size_t cbytes = (size_t)b->n_rows * Hkv * kCounterStride * sizeof(int32_t);
     if (p->counters.cap < cbytes) {
         st = p->counters.ensure(cbytes);
         if (st) return st;

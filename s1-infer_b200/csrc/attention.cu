@@ -476,7 +476,7 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, 
     }
     if (rm.n_split == 1) signal_done(p);
     if (p.counters && rm.n_split > 1)
-        finish_split_row(p, item.row, h, rm.n_split, G, D,
+        finish_split_row(p, item.row, h, item.split, rm.n_split, G, D,
                          reinterpret_cast<int*>(smem + C::kRing + NW * C::kPFloats * 4 + NW * NS * 8),
                          reinterpret_cast<float*>(smem), C::kRing / 4);  // the rings are free by now
 }

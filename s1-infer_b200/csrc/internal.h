@@ -103,6 +103,15 @@ int* device_error_word(int device);
 // (noalloc.cu); *flags = 0 if that entry point never ran there.
 int noalloc_take_error(int device, int* flags);
 
+// Split-K merging (combine.cuh): rows of up to kMergeGroup splits are
+// merged by one CTA; longer rows in two levels (groups of kMergeGroup
+// splits, then the groups).  A row has at most kMaxSplitsPerRow splits, so
+// its (row, KV head) owns kCounterStride arrival counters: the row's, then
+// one per group.
+constexpr int kMergeGroup = 16;
+constexpr int kMaxSplitsPerRow = 256;
+constexpr int kCounterStride = 1 + kMaxSplitsPerRow / kMergeGroup;
+
 // -------------------------------------------------------- device structs --
 // One query row of attention: its sequence's block-table row, the number
 // of tokens it attends to (causal limit + 1), how many split-K items cover
@@ -145,7 +154,7 @@ struct AttnParams {
     int32_t layer;
     float scale_log2;      // log2(e) / sqrt(D)
     int* err;
-    int32_t* counters;     // [n_rows][Hkv] arrivals of split CTAs, zero between launches;
+    int32_t* counters;     // [n_rows][Hkv][kCounterStride] arrivals of split CTAs, zero between launches;
                            // NULL = partials are merged by a separate combine launch
     // Output placement and the optional exchange of finished rows with peer
     // GPUs (KV-head sharding): row r, local head j goes to

@@ -18,7 +18,12 @@ Writes:
                   512, 64 decode steps): SHA-256 of every output, a few
                   outputs as values, the block table
 
-    python tests/golden/make_golden.py [--only-full]
+  logits.npz      final logits of the reference's own model code over a
+                  seeded random-weight Qwen3-0.6B-shaped model
+                  (tests/cpp/logits_parity.cpp): argmax, SHA-256 and the 32
+                  largest logits of each of 8 cached decode steps
+
+    python tests/golden/make_golden.py [--only-full | --only-logits]
 """
 from __future__ import annotations
 
@@ -157,6 +162,42 @@ def make_full(name):
     np.savez_compressed(os.path.join(HERE, f"{name}_full.npz"), **fx)
 
 
+LOGITS_ARGS = {"prompt": 64, "steps": 8, "vocab": 151936, "seed": 1}
+
+
+def read_logits(path):
+    """(argmax [steps], logits [steps, vocab]) of a logits_parity output."""
+    raw = np.fromfile(path, np.int32)
+    steps, vocab = int(raw[0]), int(raw[1])
+    rec = raw[2:].reshape(steps, 1 + vocab)
+    return rec[:, 0].copy(), rec[:, 1:].copy().view(np.float32)
+
+
+def make_logits():
+    """The reference's final logits over the seeded random-weight model
+    (oracle/_ref/logits_ref, tests/cpp/logits_parity.cpp) in both modes:
+    per step the argmax, the SHA-256 of the logits and the 32 largest."""
+    import hashlib
+    import subprocess
+    import tempfile
+    exe = os.path.join(ROOT, "oracle", "_ref", "logits_ref")
+    subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "logits"], check=True)
+    a = LOGITS_ARGS
+    out = {k: np.int64(v) for k, v in a.items()}
+    for mode in ("f32", "int8"):
+        with tempfile.TemporaryDirectory() as d:
+            path = os.path.join(d, "l.bin")
+            subprocess.run([exe, mode, str(a["prompt"]), str(a["steps"]), str(a["vocab"]), str(a["seed"]), path],
+                           check=True, capture_output=True)
+            am, lg = read_logits(path)
+        top = np.argsort(-lg, axis=1, kind="stable")[:, :32]
+        out[f"{mode}/argmax"] = am
+        out[f"{mode}/sha256"] = np.stack([np.frombuffer(hashlib.sha256(r.tobytes()).digest(), np.uint8) for r in lg])
+        out[f"{mode}/top_idx"] = top.astype(np.int32)
+        out[f"{mode}/top_val"] = np.take_along_axis(lg, top, axis=1)
+    np.savez_compressed(os.path.join(HERE, "logits.npz"), **out)
+
+
 def main():
     O.build()
     if not O.ref_available():
@@ -164,6 +205,9 @@ def main():
     if "--only-full" in sys.argv:
         for name in S.FULL_SCENARIOS:
             make_full(name)
+        return
+    if "--only-logits" in sys.argv:
+        make_logits()
         return
     make_rope()
     make_pool_ops()
@@ -173,6 +217,7 @@ def main():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **S.flatten(res, name))
     for name in S.FULL_SCENARIOS:
         make_full(name)
+    make_logits()
     print("fixtures written to", HERE)
 
 
