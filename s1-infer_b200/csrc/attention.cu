@@ -619,7 +619,7 @@ int launch_attention(s1kv_pool* pool, const AttnParams& p, int dtype, cudaStream
     const int G = p.Hq / p.Hkv;
     if (p.table && pool->tmap_sw_ok && p.items && decode_mma_supported(dtype, p.D, G, p.block_size)) {
         // bf16 K/V, head_dim 128: tensor-core decode, then the shared combine
-        int st = launch_decode_mma(p, pool->tmap_k_sw, pool->tmap_v_sw, stream);
+        int st = launch_decode_mma(p, pool->tmap_k_blk, pool->tmap_v_blk, stream);
         if (st || p.counters) return st;
         combine_kernel<<<dim3((unsigned)p.n_rows, (unsigned)p.Hkv), 128, 0, stream>>>(p, G);
         g_launches++;
@@ -680,6 +680,24 @@ int make_tensor_maps(s1kv_pool* p) {
                                 strides, box_sw, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
             if (r != CUDA_SUCCESS) return set_error(S1KV_ECUDA, "s1kv: cuTensorMapEncodeTiled (swizzled) failed (%d)", (int)r);
+        }
+        // The bf16 decode kernel takes a whole block of one KV head in one
+        // copy: dimensions (64 elements, slot, half of the row, head, layer),
+        // box (64, 16, 2, 1, 1).  Shared memory receives the two 128-byte
+        // halves of the 16 rows one after the other, the layout of two
+        // (64, 1, 16, 1) boxes above, with one TMA operation instead of two
+        // (measured 1-2% faster on one-KV-head rows of 131,072 tokens).
+        cuuint64_t dims5[5] = {64, (cuuint64_t)p->num_slots, 2, (cuuint64_t)p->desc.num_kv_heads,
+                               (cuuint64_t)p->desc.num_layers};
+        cuuint64_t strides5[4] = {(cuuint64_t)p->desc.num_kv_heads * D * e, 64 * e, (cuuint64_t)D * e,
+                                  (cuuint64_t)p->num_slots * p->desc.num_kv_heads * D * e};
+        cuuint32_t box5[5] = {64, 16, 2, 1, 1};
+        cuuint32_t estr5[5] = {1, 1, 1, 1, 1};
+        for (int which = 0; which < 2; which++) {
+            CUresult r = encode(which ? &p->tmap_v_blk : &p->tmap_k_blk, dt, 5, which ? (void*)p->v : (void*)p->k,
+                                dims5, strides5, box5, estr5, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) return set_error(S1KV_ECUDA, "s1kv: cuTensorMapEncodeTiled (block) failed (%d)", (int)r);
         }
         p->tmap_sw_ok = true;
     }

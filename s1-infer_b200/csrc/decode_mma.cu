@@ -16,9 +16,10 @@
 // 16-token tile costs 16 ldmatrix, 4 movmatrix and 32 mma per warp.
 //   * Token-major products, so the 8 heads (or fewer) of a group fill the
 //     N = 8 side of m16n8k16 and no M rows are padding:
-//     S^T[token, head] = K Q^T with M = 16 tokens, K = 16 dims; K tiles
-//     arrive by TMA in the 128-byte-swizzled layout (two 64-element halves
-//     per row), so ldmatrix reads them without bank conflicts.
+//     S^T[token, head] = K Q^T with M = 16 tokens, K = 16 dims; a K (or V)
+//     tile arrives by one TMA copy in the 128-byte-swizzled layout (the two
+//     64-element halves of the rows one after the other), so ldmatrix reads
+//     it without bank conflicts.
 //   * The score fragment of a thread (tokens g, g+8; heads 2t, 2t+1) turns
 //     into P's B fragment of O^T += V^T P^T (head g; tokens 2t, 2t+1,
 //     2t+8, 2t+9) by one movmatrix transpose per 8x8 half, so P never
@@ -76,11 +77,12 @@ __device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t phase) {
     }
     return false;
 }
-__device__ __forceinline__ void tma4(void* dst, const CUtensorMap* m, uint64_t* b, int c0, int c1, int c2, int c3) {
+__device__ __forceinline__ void tma5(void* dst, const CUtensorMap* m, uint64_t* b, int c0, int c1, int c2, int c3,
+                                     int c4) {
     asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
-        "[%6];" ::"r"(su32(dst)),
-        "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(su32(b))
+        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, %6}], "
+        "[%7];" ::"r"(su32(dst)),
+        "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(su32(b))
         : "memory");
 }
 
@@ -179,10 +181,8 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
         const int s = k % kNS;
         uint8_t* dst = ring + s * kStageBytes;
         bar_expect(&bar[s], kStageBytes);
-        tma4(dst, &tmK, &bar[s], 0, h, row, p.layer);
-        tma4(dst + kBoxBytes, &tmK, &bar[s], 64, h, row, p.layer);
-        tma4(dst + kTileBytes, &tmV, &bar[s], 0, h, row, p.layer);
-        tma4(dst + kTileBytes + kBoxBytes, &tmV, &bar[s], 64, h, row, p.layer);
+        tma5(dst, &tmK, &bar[s], 0, row, 0, h, p.layer);  // both halves of the block's 16 rows
+        tma5(dst + kTileBytes, &tmV, &bar[s], 0, row, 0, h, p.layer);
     };
     for (int k = 0; k < min(kNS, my_tiles); k++) {
         const int row = __shfl_sync(kFull, my_row, k);

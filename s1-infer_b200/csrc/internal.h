@@ -109,8 +109,8 @@ int noalloc_take_error(int device, int* flags);
 // its (row, KV head) owns kCounterStride arrival counters: the row's, then
 // one per group.
 constexpr int kMergeGroup = 16;
-constexpr int kMaxSplitsPerRow = 256;
-constexpr int kCounterStride = 1 + kMaxSplitsPerRow / kMergeGroup;
+constexpr int kMaxSplitsPerRow = 64;
+constexpr int kCounterStride = 1 + (kMaxSplitsPerRow + kMergeGroup - 1) / kMergeGroup;
 
 // -------------------------------------------------------- device structs --
 // One query row of attention: its sequence's block-table row, the number
@@ -287,6 +287,8 @@ struct s1kv_pool {
     bool tmap_ok = false;
     CUtensorMap tmap_k_sw{};  // 128B-swizzled 64-element boxes (tensor-core prefill)
     CUtensorMap tmap_v_sw{};
+    CUtensorMap tmap_k_blk{}; // one KV head of one block in one box, both 128B-swizzled halves (bf16 decode)
+    CUtensorMap tmap_v_blk{};
     bool tmap_sw_ok = false;
     // host bookkeeping
     std::vector<int32_t> free_list;   // LIFO, back() allocated first

@@ -379,14 +379,23 @@ def test_cfg4_rank_shape_131072_token_rows(s1kv, oracle, cuda):
     def ref(i):
         kk = np.concatenate([kb[i * CTX:(i + 1) * CTX], kr1[i:i + 1]])
         vv = np.concatenate([vb[i * CTX:(i + 1) * CTX], v1b[i:i + 1]])
-        return oracle.gqa_attention(qr[i:i + 1], kk, vv, Hq, Hkv, D)
+        return oracle.gqa_attention(qr[i:i + 1], kk, vv, Hq, Hkv, D), np_causal_gqa(qr[i:i + 1], kk, vv, Hq, Hkv)
 
-    refs = pmap(ref, range(B))
-    errs = [rel_err(out[i:i + 1], refs[i]) for i in range(B)]
+    refs = pmap(ref, range(B), workers=2)
+    # Over 131,073 keys the oracle's own fp32 sums (the reference's
+    # sequential loops) are off the exact result by ~1.5-2e-5 of the output
+    # scale, so the kernel is held to 2e-5 against the float64 evaluation of
+    # the same arithmetic, and to 2e-5 plus the oracle's own error against
+    # the oracle.
+    err64 = [rel_err(out[i:i + 1], refs[i][1]) for i in range(B)]
+    err_or = [rel_err(out[i:i + 1], refs[i][0]) for i in range(B)]
+    or64 = [rel_err(refs[i][0], refs[i][1]) for i in range(B)]
     splits = (CTX + 1 + split_tokens - 1) // split_tokens
     print(f"cfg4 rank shape: 4 x 131073 tokens, {splits} splits of {split_tokens} tokens per row, "
-          f"{n_items} work items; rel err {max(errs):.2e}")
-    assert max(errs) <= TOL_F32, errs
+          f"{n_items} work items; rel err vs float64 {max(err64):.2e}, vs the oracle {max(err_or):.2e} "
+          f"(the oracle vs float64: {max(or64):.2e})")
+    assert max(err64) <= TOL_F32, err64
+    assert all(e <= TOL_F32 + o for e, o in zip(err_or, or64)), (err_or, or64)
     for s in seqs:
         assert pool.length(s) == CTX + 1
     assert pool.check_device() == 0

@@ -248,18 +248,18 @@ def test_batched_decode_vs_oracle(s1kv, oracle, cuda, dtype, shape):
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 def test_long_rows_capped_splits_vs_oracle(s1kv, oracle, cuda, dtype):
-    """Rows long enough for the split planner's cap of 256 splits per row
-    (one KV head, 8 query heads; 40,000 tokens = 2,500 tiles -> splits of 10
-    tiles, 250 of them): the row merges in two levels -- the last CTA of
-    each group of 16 splits merges the group (the last group holds 10), then
-    the last group merges the 16 group results (16-byte loads, eight
-    partials in flight).  The 9,000-token row takes 57 splits (4 groups),
-    the 300-token row 2 (one level).  Each row against the oracle's
-    contiguous GQA attention, 2e-5 x max |ref| (bf16: on the bf16-rounded
-    K/V)."""
+    """Rows long enough for the split planner's cap of 64 splits per row
+    (one KV head, 8 query heads; 40,000 tokens = 2,500 tiles -> splits of 40
+    tiles, 63 of them): the row merges in two levels -- the last CTA of
+    each group of 16 splits merges the group (the last group holds 15), then
+    the last group merges the 4 group results (16-byte loads, eight
+    partials in flight).  The 10,800-token row takes 17 splits (a group of
+    16 and a group of one), the 9,000-token row 15 (one level), the
+    300-token row one.  Each row against the oracle's contiguous GQA
+    attention, 2e-5 x max |ref| (bf16: on the bf16-rounded K/V)."""
     import torch
     Hq, Hkv, D, bs = 8, 1, 128, 16
-    ctx = [40000, 9000, 300]
+    ctx = [40000, 10800, 9000, 300]
     B = len(ctx)
     rng = np.random.default_rng(31)
     k = [rng.standard_normal((c, Hkv, D), dtype=np.float32) for c in ctx]
@@ -274,8 +274,8 @@ def test_long_rows_capped_splits_vs_oracle(s1kv, oracle, cuda, dtype):
     with pool.batch(seqs, [0] * B, [1] * B) as b:
         split_tokens, _ = b.plan()
         out = host(b.attention(0, torch.from_numpy(q).cuda()))
-    assert split_tokens == 10 * 16
-    assert [(c + split_tokens - 1) // split_tokens for c in ctx] == [250, 57, 2]
+    assert split_tokens == 40 * 16
+    assert [(c + split_tokens - 1) // split_tokens for c in ctx] == [63, 17, 15, 1]
     for s in range(B):
         kk = oracle.bf16_round(k[s]) if dtype == "bf16" else k[s]
         vv = oracle.bf16_round(v[s]) if dtype == "bf16" else v[s]
