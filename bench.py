@@ -624,23 +624,30 @@ def run_cfg5(s1kv, torch, rank, world, steps=100, warmup=20):
     kbuf = torch.randn((cap, HKV, D), device="cuda", generator=gen)
     vbuf = torch.randn((cap, HKV, D), device="cuda", generator=gen)
     qbuf = torch.randn((max_running, HQ, D), device="cuda", generator=gen)
-    host = [0.0]
+    # host[0]: wall time of the bookkeeping calls (which includes waiting for
+    # a staging buffer the GPU still reads when the host is ahead); host[1]:
+    # the CPU time this thread spent in them; host[2]: CPU time of the whole
+    # step's issue (bookkeeping and the 64 per-layer calls)
+    host = [0.0, 0.0, 0.0]
 
     def step():
-        h0 = time.perf_counter()
+        h0, c0, s0 = time.perf_counter(), time.thread_time(), time.thread_time()
         plan = drv.plan()
         b = drv.open(plan)
         host[0] += time.perf_counter() - h0
+        host[1] += time.thread_time() - c0
         assert plan.n_tokens <= cap
         for layer in range(layers):
             q = qbuf[:plan.n_rows] if plan.n_rows else None
             qr = b.rope_append(layer, kbuf[:plan.n_tokens], vbuf[:plan.n_tokens], q=q)
             if plan.n_rows:
                 b.attention(layer, qr)
-        h0 = time.perf_counter()
+        h0, c0 = time.perf_counter(), time.thread_time()
         b.end()
         drv.close(plan)
         host[0] += time.perf_counter() - h0
+        host[1] += time.thread_time() - c0
+        host[2] += time.thread_time() - s0
 
     step()
     rng = np.random.default_rng(7 + rank)
@@ -652,7 +659,7 @@ def run_cfg5(s1kv, torch, rank, world, steps=100, warmup=20):
     barrier(torch, world)
     s0 = dict(drv.stats)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    host[0] = 0.0
+    host[:] = [0.0, 0.0, 0.0]
     t0 = time.perf_counter()
     ev0.record()
     for _ in range(steps):
@@ -662,6 +669,26 @@ def run_cfg5(s1kv, torch, rank, world, steps=100, warmup=20):
     wall_ms = (time.perf_counter() - t0) * 1e3
     gpu_ms = ev0.elapsed_time(ev1)
     d = {k: drv.stats[k] - s0.get(k, 0) for k in drv.stats}
+    # The bookkeeping alone: further steps with the device drained before
+    # each bookkeeping call, so that no wait for a staging buffer still in
+    # use (the host running ahead of the GPU) is counted.
+    idle = []
+    for _ in range(20):
+        torch.cuda.synchronize()
+        c0 = time.perf_counter()
+        plan = drv.plan()
+        b = drv.open(plan)
+        c1 = time.perf_counter()
+        for layer in range(layers):
+            qr = b.rope_append(layer, kbuf[:plan.n_tokens], vbuf[:plan.n_tokens],
+                               q=qbuf[:plan.n_rows] if plan.n_rows else None)
+            if plan.n_rows:
+                b.attention(layer, qr)
+        torch.cuda.synchronize()
+        c2 = time.perf_counter()
+        b.end()
+        drv.close(plan)
+        idle.append((c1 - c0) + (time.perf_counter() - c2))
     st = pool.stats()
     assert pool.check_device() == 0
     pool.close()
@@ -677,6 +704,9 @@ def run_cfg5(s1kv, torch, rank, world, steps=100, warmup=20):
             "steps": steps, "decode_tok_s": dec / (wall_max * 1e-3), "appended_tok_s": app / (wall_max * 1e-3),
             "ms_per_step": wall_max / steps, "gpu_ms_per_step": gpu_ms / steps,
             "host_bookkeeping_ms_per_step": host[0] * 1e3 / steps,
+            "host_bookkeeping_cpu_ms_per_step": host[1] * 1e3 / steps,
+            "host_issue_cpu_ms_per_step": host[2] * 1e3 / steps,
+            "host_bookkeeping_idle_ms_per_step": float(np.median(idle)) * 1e3,
             "per_gpu_in_window": {k: d.get(k, 0) for k in ("admitted", "retired", "deferred", "preempted",
                                                              "prefix_hit_tokens", "decode_tokens", "appended_tokens")},
             "evictions_total": st["evictions"], "occupancy": 1.0 - st["num_free"] / max_blocks}
@@ -933,7 +963,10 @@ def run_ours(args):
                      "nccl_tok_s": r(cfg4["nccl_allgather"]["tok_s"]), "scaling": "strong"}
     if cfg5 is not None:
         v["cfg5"] = {"decode_tok_s": r(cfg5["decode_tok_s"]), "ms_per_step": r(cfg5["ms_per_step"]),
-                     "gpu_ms": r(cfg5["gpu_ms_per_step"]), "host_ms": r(cfg5["host_bookkeeping_ms_per_step"]),
+                     "gpu_ms": r(cfg5["gpu_ms_per_step"]), "host_wall_ms": r(cfg5["host_bookkeeping_ms_per_step"]),
+                     "host_cpu_ms": r(cfg5["host_bookkeeping_cpu_ms_per_step"]),
+                     "host_idle_ms": r(cfg5["host_bookkeeping_idle_ms_per_step"]),
+                     "issue_cpu_ms": r(cfg5["host_issue_cpu_ms_per_step"]),
                      "evictions": cfg5["evictions_total"]}
     if int8 is not None:
         m1, m8 = int8["M1"], int8["M8"]
