@@ -482,7 +482,7 @@ def run_cfg3(s1kv, torch, rank, reps=10, n=256):
 CFG4_B, CFG4_CTX, CFG4_HQ, CFG4_HKV, CFG4_LAYERS = 4, 131072, 64, 8, 80
 
 
-def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3):
+def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3, shard=None, max_layers=CFG4_LAYERS):
     """cfg4, KV-head-sharded long-context decode: 4 sequences at context
     131072, Hq 64 / Hkv 8 / D 128, bf16 K/V, 80 layers, blocks scattered over
     a pool of 1.1x need (permutation seed 3).  Rank r of N keeps only KV heads
@@ -495,14 +495,16 @@ def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3):
     (N = 1), fewer layers are timed and the step figures are scaled to 80.
     K/V are seeded normal values (synthetic post-RoPE keys)."""
     B, CTX, hq_all, hkv_all = CFG4_B, CFG4_CTX, CFG4_HQ, CFG4_HKV
-    kv_lo, kv_hi, q_lo, q_hi = s1kv.head_shard(world, rank, hkv_all, hq_all)
+    # shard (profiling case, one process): rank 0's share of a `shard`-GPU
+    # run, timed alone on this GPU
+    kv_lo, kv_hi, q_lo, q_hi = s1kv.head_shard(shard or world, rank, hkv_all, hq_all)
     hkv, hq = kv_hi - kv_lo, q_hi - q_lo
-    need = B * ((CTX + steps + warmup + 2 + BS - 1) // BS)
+    need = B * ((CTX + 2 * (warmup + steps + 3) + BS - 1) // BS)  # two modes of warm-up, timed and breakdown steps
     max_blocks = int(need * 1.1)
     per_layer = max_blocks * BS * hkv * D * 2 * 2
     torch.cuda.empty_cache()
     free, _ = torch.cuda.mem_get_info()
-    layers = int(min(CFG4_LAYERS, (free - 16e9) // per_layer))
+    layers = int(min(max_layers, (free - 16e9) // per_layer))
     layers = int(-max_over_ranks(torch, world, -layers))  # every rank times the same layers
     order = np.random.default_rng(3).permutation(max_blocks).astype(np.int32)
     pool = s1kv.Pool(layers, hkv, D, max_blocks, BS, dtype="bf16", initial_free_list=order, max_seqs=8)
@@ -521,6 +523,7 @@ def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3):
     kn = torch.randn((layers, B, hkv, D), device="cuda", generator=gen)
     vn = torch.randn((layers, B, hkv, D), device="cuda", generator=gen)
     q_rot = torch.empty((B, hq, D), device="cuda")
+    q_next = torch.empty((B, hq, D), device="cuda")
     out = torch.empty((B, hq, D), device="cuda")
     gbuf = torch.empty((world, B, hq, D), device="cuda")
     nxt = (rank + 1) % world
@@ -551,7 +554,9 @@ def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3):
                     full = s1kv.gather_heads(out, world, buf=gbuf)  # [B, 64, 128] token-major on every rank
                 if ev is not None:
                     ev[layer][2].record()
-                q = full[:, nxt * hq:(nxt + 1) * hq].contiguous()
+                # the next layer's queries of this rank's heads: another
+                # rank's outputs (one copy into a buffer made once)
+                q = q_next.copy_(full[:, nxt * hq:(nxt + 1) * hq])
 
     res = {}
     for mode in ("nccl", "fused"):
@@ -561,21 +566,32 @@ def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3):
         barrier(torch, world)
         torch.cuda.synchronize()
         ctx_before = [pool.length(s) for s in seqs]
-        evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(layers)] for _ in range(steps)]
+        # the timed steps carry no per-layer events (an event between two
+        # kernels ends their programmatic launch overlap)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
+        h0 = time.perf_counter()
         for i in range(steps):
-            step(evs[i], fused=fused)
+            step(fused=fused)
+        issue_us = (time.perf_counter() - h0) * 1e6 / (steps * layers)  # host time to issue a layer
         t1.record()
         torch.cuda.synchronize()
         elapsed = max_over_ranks(torch, world, t0.elapsed_time(t1))
-        attn_ms = float(np.mean([evs[i][l][0].elapsed_time(evs[i][l][1]) for i in range(steps) for l in range(layers)]))
-        xchg_ms = float(np.mean([evs[i][l][1].elapsed_time(evs[i][l][2]) for i in range(steps) for l in range(layers)]))
-        res[mode] = (elapsed, max_over_ranks(torch, world, attn_ms), max_over_ranks(torch, world, xchg_ms), ctx_before)
+        # per-layer breakdown: a few more steps with an event pair around
+        # each attention call and the exchange that follows it
+        n_ev = min(steps, 3)
+        evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(layers)] for _ in range(n_ev)]
+        for i in range(n_ev):
+            step(evs[i], fused=fused)
+        torch.cuda.synchronize()
+        attn_ms = float(np.mean([evs[i][l][0].elapsed_time(evs[i][l][1]) for i in range(n_ev) for l in range(layers)]))
+        xchg_ms = float(np.mean([evs[i][l][1].elapsed_time(evs[i][l][2]) for i in range(n_ev) for l in range(layers)]))
+        res[mode] = (elapsed, max_over_ranks(torch, world, attn_ms), max_over_ranks(torch, world, xchg_ms), ctx_before,
+                     max_over_ranks(torch, world, issue_us))
     s1kv.device_check(torch.cuda.current_device())
     barrier(torch, world)  # no rank frees its exchange buffer while a peer may still hold it open
     ex.close()
-    elapsed, attn_ms, gather_ms, ctx_before = res["fused"]
+    elapsed, attn_ms, gather_ms, ctx_before, issue_us = res["fused"]
     # algorithmic bytes of one layer's attention on this GPU: K and V of the
     # local heads once, q in and out (fp32), block ids
     ctx_mid = [c + (steps + 1) // 2 for c in ctx_before]
@@ -594,7 +610,7 @@ def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3):
             "scaling": "strong", "layers_timed": layers, "steps": steps,
             "ms_per_step_80_layers": step_ms_80, "tok_s": B / (step_ms_80 * 1e-3),
             "ms_per_layer": elapsed / steps / layers, "attn_ms_per_layer": attn_ms,
-            "exchange_wait_ms_per_layer": gather_ms,
+            "exchange_wait_ms_per_layer": gather_ms, "host_issue_us_per_layer": issue_us,
             "attn_bytes_per_layer_per_gpu": attn_bytes, "kv_gbs_per_gpu": attn_bytes / (attn_ms * 1e-3) / 1e9}
 
 
@@ -868,7 +884,8 @@ def run_ours(args):
         res[dtype] = run_variant(s1kv, torch, dtype, share, args.steps, args.warmup, rank, world,
                                  timed_e2e=not args.no_e2e, sample_clocks=(dtype == "f32"))
     cfg3 = run_cfg3(s1kv, torch, rank, n=args.cfg3_seqs) if not args.only or args.only == "cfg3" else None
-    cfg4 = run_cfg4(s1kv, torch, rank, world) if not args.only or args.only == "cfg4" else None
+    cfg4 = run_cfg4(s1kv, torch, rank, world, shard=args.cfg4_shard, max_layers=args.cfg4_layers) \
+        if not args.only or args.only == "cfg4" else None
     cfg5 = run_cfg5(s1kv, torch, rank, world) if not args.only or args.only == "cfg5" else None
     int8 = run_int8(s1kv, torch, rank, cpu_sample=(world == 1 and not args.no_cpu_baseline)) \
         if not args.only or args.only == "int8" else None
@@ -960,6 +977,7 @@ def run_ours(args):
         v["cfg4"] = {"tok_s": r(cfg4["tok_s"]), "ms_per_step": r(cfg4["ms_per_step_80_layers"]),
                      "layers_timed": cfg4["layers_timed"], "attn_ms": r(cfg4["attn_ms_per_layer"]),
                      "frac": r(cfg4["kv_gbs_per_gpu"] / peak), "wait_ms": r(cfg4["exchange_wait_ms_per_layer"]),
+                     "issue_us": r(cfg4["host_issue_us_per_layer"]),
                      "nccl_tok_s": r(cfg4["nccl_allgather"]["tok_s"]), "scaling": "strong"}
     if cfg5 is not None:
         v["cfg5"] = {"decode_tok_s": r(cfg5["decode_tok_s"]), "ms_per_step": r(cfg5["ms_per_step"]),
@@ -1052,6 +1070,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cfg3-seqs", type=int, default=256, help="profiling case: sequences of the cfg3 variant")
     ap.add_argument("--detail", help="also write every figure of the run, unrounded, to this JSON file")
+    ap.add_argument("--cfg4-shard", type=int, default=None,
+                    help="profiling case: the cfg4 variant as one GPU's KV-head shard of an N-GPU run")
+    ap.add_argument("--cfg4-layers", type=int, default=CFG4_LAYERS, help="profiling case: layers of the cfg4 variant")
     args = ap.parse_args()
     globals()["LAYERS"] = args.layers
     if args.warmup < 3:

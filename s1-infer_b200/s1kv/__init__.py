@@ -711,14 +711,18 @@ class PeerExchange:
     def output(self, epoch, rows=None):
         """The gathered [rows, heads_total, head_dim] of `epoch` (a view of
         the exchange's memory; valid until the slot is reused two epochs
-        later or the exchange is closed)."""
+        later or the exchange is closed).  The two slots' tensors are made
+        once: a decode loop calls this every layer."""
         import torch
-        ptr = self.L.s1kv_exchange_buffer(self.h, epoch)
-        t = torch.as_tensor(_DeviceArray(ptr, self.shape), device="cuda")
+        if not hasattr(self, "_slots"):
+            self._slots = [torch.as_tensor(_DeviceArray(self.L.s1kv_exchange_buffer(self.h, e), self.shape),
+                                           device="cuda") for e in (0, 1)]
+        t = self._slots[epoch & 1]
         return t if rows is None else t[:rows]
 
     def close(self):
         if getattr(self, "h", None):
+            self._slots = None
             self.L.s1kv_exchange_destroy(self.h)
             self.h = None
 
