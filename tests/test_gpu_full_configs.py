@@ -23,7 +23,8 @@ Tolerances: bytes, slots, tables, refcounts bit-exact; fp32 attention (and
 bf16-storage decode against the oracle on the same bf16-rounded K/V) within
 2e-5 x max|ref|; bf16 storage against the fp32 oracle within 1e-2; the
 tensor-core prefill (bf16 Q and P) within PREFILL_TOL of the oracle on the
-same rounded K/V.  Measured errors are printed (pytest -s)."""
+same rounded K/V, with a median over the 256 sequences within
+PREFILL_MEDIAN_TOL.  Measured errors are printed (pytest -s)."""
 import concurrent.futures as cf
 import os
 import sys
@@ -40,6 +41,7 @@ pytestmark = pytest.mark.gpu
 TOL_F32 = 2e-5
 TOL_BF16 = 1e-2
 PREFILL_TOL = 1e-2
+PREFILL_MEDIAN_TOL = 5e-3
 THREADS = min(32, os.cpu_count() or 1)
 
 
@@ -322,6 +324,9 @@ def test_cfg3_full_256_forks_prefill_and_decode(s1kv, oracle, cuda):
     print(f"cfg3 prefill: 256 seqs x suffix U[64,512] over 2050 + suffix keys, bf16 K/V; rel err vs oracle "
           f"max {max(errs):.2e}, median {np.median(errs):.2e}")
     assert max(errs) <= PREFILL_TOL, max(errs)
+    # the bf16 narrowing of Q and P gives 3-7e-3 per sequence (median 3.3e-3
+    # measured); a median far above that is a regression, not rounding
+    assert np.median(errs) <= PREFILL_MEDIAN_TOL, np.median(errs)
     # two decode steps over the shared prefix blocks
     worst = 0.0
     for _ in range(dec_steps):

@@ -2,7 +2,9 @@
 of several query rows per sequence over bf16 K/V, against the CPU oracle
 (src/nn/attention.cpp:128-239 restated) run on the same bf16-rounded K/V.
 Q and the softmax weights enter the tensor cores as bf16, so the bound is
-the bf16-storage tolerance: max |out - ref| <= 1e-2 * max |ref|."""
+the bf16-storage tolerance: max |out - ref| <= 1e-2 * max |ref|; the
+measured errors (printed, pytest -s) are 3-7e-3 (the full cfg3 prefill in
+test_gpu_full_configs.py: median 3.3e-3, max 6.9e-3 over 256 sequences)."""
 import numpy as np
 import pytest
 
@@ -50,7 +52,9 @@ def test_prefill_tc_matches_oracle(s1kv, oracle, cuda, Hq, Hkv):
     qlens = [64, 100, 33, 129, 1, 16]
     out, ref = run_case(s1kv, oracle, cuda, Hq, Hkv, totals, qlens, seed=Hq + Hkv)
     assert np.isfinite(out).all()
-    assert rel_err(out, ref) <= TOL_BF16, rel_err(out, ref)
+    err = rel_err(out, ref)
+    print(f"prefill Hq {Hq} Hkv {Hkv}: rel err {err:.2e}")
+    assert err <= TOL_BF16, err
 
 
 def test_prefill_tc_long_prefix_many_sequences(s1kv, oracle, cuda):
@@ -58,4 +62,6 @@ def test_prefill_tc_long_prefix_many_sequences(s1kv, oracle, cuda):
     qlens = [int(x) for x in rng.integers(1, 300, size=12)]
     totals = [1500 + q for q in qlens]
     out, ref = run_case(s1kv, oracle, cuda, 32, 8, totals, qlens, seed=3)
-    assert rel_err(out, ref) <= TOL_BF16, rel_err(out, ref)
+    err = rel_err(out, ref)
+    print(f"prefill, 12 sequences over a 1500-token prefix: rel err {err:.2e}")
+    assert err <= TOL_BF16, err
