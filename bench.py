@@ -538,25 +538,26 @@ def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3, shard=None, max_layer
                 bt.rope_append(layer, kn[layer], vn[layer], q=q, q_out=q_rot)
                 if ev is not None:
                     ev[layer][0].record()
+                # the next layer's queries of this rank's heads are another
+                # rank's outputs
                 if fused:
                     # the decode kernels store every finished row into all
-                    # ranks' token-major buffers over NVLink, then signal
+                    # ranks' token-major buffers over NVLink, then signal;
+                    # one kernel waits for every rank and copies the next
+                    # layer's query heads out
                     epoch[0] += 1
                     ex.attention(bt, layer, q_rot, q_lo, epoch[0])
                     if ev is not None:
                         ev[layer][1].record()
-                    ex.wait(epoch[0])
-                    full = ex.output(epoch[0])
+                    q = ex.wait_copy(epoch[0], nxt * hq, hq, q_next)
                 else:
                     bt.attention(layer, q_rot, out=out)
                     if ev is not None:
                         ev[layer][1].record()
                     full = s1kv.gather_heads(out, world, buf=gbuf)  # [B, 64, 128] token-major on every rank
+                    q = q_next.copy_(full[:, nxt * hq:(nxt + 1) * hq])
                 if ev is not None:
                     ev[layer][2].record()
-                # the next layer's queries of this rank's heads: another
-                # rank's outputs (one copy into a buffer made once)
-                q = q_next.copy_(full[:, nxt * hq:(nxt + 1) * hq])
 
     res = {}
     for mode in ("nccl", "fused"):

@@ -220,7 +220,9 @@ int s1kv_prefix_load_v1(s1kv_pool* pool, uint64_t seq, const char* path, int32_t
  * batch's attention for this rank's heads and stores each finished row into
  * its place in every rank's slot over NVLink, then signals `epoch`;
  * s1kv_exchange_wait (device, bounded: sets the timeout bit of the error word
- * after about a second) makes the stream wait until all ranks signalled it.
+ * after about a second) makes the stream wait until all ranks signalled it;
+ * it is a programmatic dependent launch, resident while this rank's decode
+ * kernel finishes, and polls only after that kernel completed.
  * Epochs increase by one per layer step. */
 typedef struct s1kv_exchange s1kv_exchange;
 int s1kv_exchange_create(int device, int32_t rank, int32_t world, int64_t slot_floats, s1kv_exchange** out);
@@ -236,6 +238,15 @@ int s1kv_exchange_open_local(s1kv_exchange* ex, void* const* bases);
 /* Device address of the slot `epoch` uses: [rows][heads_total][head_dim]. */
 float* s1kv_exchange_buffer(const s1kv_exchange* ex, uint32_t epoch);
 int s1kv_exchange_wait(s1kv_exchange* ex, uint32_t epoch, void* stream);
+/* s1kv_exchange_wait, then (in the same kernel) a copy of heads [head0,
+ * head0 + n_heads) of every row of the epoch's slot, laid out [rows]
+ * [heads_total][head_dim] as s1kv_batch_attention_exchange wrote it, into
+ * dst [rows][n_heads][head_dim] (device, 16-byte aligned; head_dim a
+ * multiple of 4).  For a consumer that wants one contiguous head range of
+ * the gathered output, e.g. the query heads a rank feeds to its next layer.
+ * On a timeout dst is left unwritten (and the timeout bit set). */
+int s1kv_exchange_wait_copy(s1kv_exchange* ex, uint32_t epoch, int32_t rows, int32_t heads_total, int32_t head_dim,
+                            int32_t head0, int32_t n_heads, float* dst, void* stream);
 int s1kv_exchange_destroy(s1kv_exchange* ex);
 /* Decode attention of this rank's n_q_heads query heads (first global head
  * head0 of heads_total), output published through the exchange. */

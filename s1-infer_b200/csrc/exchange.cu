@@ -26,17 +26,40 @@ size_t flags_offset(int64_t slot_floats) { return (size_t)2 * slot_floats * size
 size_t done_offset(int64_t slot_floats) { return flags_offset(slot_floats) + 2 * 8 * sizeof(uint32_t); }
 size_t alloc_bytes(int64_t slot_floats) { return done_offset(slot_floats) + 256; }
 
-// Lane r waits until rank r's flag in this slot has reached `epoch`.
-__global__ void exchange_wait_kernel(const uint32_t* flags, int world, uint32_t epoch, int* err) {
-    const int r = threadIdx.x;
-    if (r >= world) return;
-    for (uint32_t i = 0; i < kWaitSpins; i++) {
-        uint32_t v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
-        if ((int32_t)(v - epoch) >= 0) return;
-        __nanosleep(64);
+// Lane r of warp 0 waits until rank r's flag in this slot has reached
+// `epoch`; then, when `dst` is set, the CTA copies heads [head0, head0 +
+// n_heads) of every row of the slot [rows][heads_total][D] into dst [rows]
+// [n_heads][D].  Launched as a programmatic dependent launch: the CTA may
+// become resident while this rank's decode kernel still runs, and waits for
+// it to complete (griddepcontrol.wait) before polling, so the only waits
+// left are on the other GPUs' kernels.
+__global__ void exchange_wait_kernel(const uint32_t* flags, int world, uint32_t epoch, int* err, const float* slot,
+                                     int rows, int heads_total, int D, int head0, int n_heads, float* dst) {
+    pdl_enter();
+    __shared__ int ok;
+    if (threadIdx.x < 32) {
+        const int r = threadIdx.x;
+        bool seen = r >= world;
+        for (uint32_t i = 0; i < kWaitSpins && !seen; i++) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
+            seen = (int32_t)(v - epoch) >= 0;
+            if (!seen) __nanosleep(64);
+        }
+        const bool all = __all_sync(0xffffffffu, seen);
+        if (threadIdx.x == 0) {
+            if (!all) atomicOr(err, kErrTimeout);
+            ok = all;
+        }
     }
-    atomicOr(err, kErrTimeout);
+    __syncthreads();
+    if (!dst || !ok) return;
+    const int per_row = n_heads * D / 4;  // float4 per row
+    for (int i = threadIdx.x; i < rows * per_row; i += blockDim.x) {
+        const int row = i / per_row, c = i % per_row;
+        reinterpret_cast<float4*>(dst)[i] =
+            reinterpret_cast<const float4*>(slot + ((int64_t)row * heads_total + head0) * D)[c];
+    }
 }
 
 }  // namespace
@@ -151,14 +174,31 @@ float* s1kv_exchange_buffer(const s1kv_exchange* ex, uint32_t epoch) {
     return reinterpret_cast<float*>(ex->base + (size_t)(epoch & 1) * ex->slot_floats * sizeof(float));
 }
 
-int s1kv_exchange_wait(s1kv_exchange* ex, uint32_t epoch, void* stream) {
+static int exchange_wait_impl(s1kv_exchange* ex, uint32_t epoch, int32_t rows, int32_t heads_total, int32_t head_dim,
+                              int32_t head0, int32_t n_heads, float* dst, void* stream) {
     if (!ex) return set_error(S1KV_EINVAL, "null exchange");
     S1KV_ON_DEVICE(ex->device);
     const uint32_t* flags = reinterpret_cast<const uint32_t*>(ex->base + flags_offset(ex->slot_floats)) + (epoch & 1) * 8;
-    exchange_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flags, ex->world, epoch, ex->d_err);
+    const float* slot = reinterpret_cast<const float*>(ex->base + (size_t)(epoch & 1) * ex->slot_floats * sizeof(float));
+    S1KV_CUDA(launch_pdl(exchange_wait_kernel, dim3(1), dim3(dst ? 256 : 32), 0, (cudaStream_t)stream, flags, ex->world,
+                         epoch, ex->d_err, slot, rows, heads_total, head_dim, head0, n_heads, dst));
     g_launches++;
     S1KV_CUDA(cudaGetLastError());
     return S1KV_OK;
+}
+
+int s1kv_exchange_wait(s1kv_exchange* ex, uint32_t epoch, void* stream) {
+    return exchange_wait_impl(ex, epoch, 0, 0, 0, 0, 0, nullptr, stream);
+}
+
+int s1kv_exchange_wait_copy(s1kv_exchange* ex, uint32_t epoch, int32_t rows, int32_t heads_total, int32_t head_dim,
+                            int32_t head0, int32_t n_heads, float* dst, void* stream) {
+    if (!ex || !dst || rows < 0 || heads_total <= 0 || head_dim <= 0 || head0 < 0 || n_heads <= 0 ||
+        head0 + n_heads > heads_total || (n_heads * head_dim) % 4 || head_dim % 4 ||
+        (int64_t)rows * heads_total * head_dim > ex->slot_floats || ((uintptr_t)dst & 15))
+        return set_error(S1KV_EINVAL, "s1kv_exchange_wait_copy: bad shape (head_dim a multiple of 4, dst 16-byte "
+                                      "aligned, rows x heads_total x head_dim within the slot)");
+    return exchange_wait_impl(ex, epoch, rows, heads_total, head_dim, head0, n_heads, dst, stream);
 }
 
 int s1kv_exchange_destroy(s1kv_exchange* ex) {

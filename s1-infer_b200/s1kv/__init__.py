@@ -113,6 +113,7 @@ SIGNATURES = {
     "s1kv_exchange_create": (C.c_int, [C.c_int, i32, i32, i64, P(vp)]),
     "s1kv_exchange_handle": (C.c_int, [vp, vp]),
     "s1kv_exchange_open": (C.c_int, [vp, vp]),
+    "s1kv_exchange_wait_copy": (C.c_int, [vp, C.c_uint32, i32, i32, i32, i32, i32, vp, vp]),
     "s1kv_exchange_base": (vp, [vp]),
     "s1kv_exchange_open_local": (C.c_int, [vp, vp]),
     "s1kv_exchange_buffer": (vp, [vp, C.c_uint32]),
@@ -707,6 +708,15 @@ class PeerExchange:
         unless `force`."""
         if self.world > 1 or force:
             check(self.L.s1kv_exchange_wait(self.h, epoch, _stream()))
+
+    def wait_copy(self, epoch, head0, n_heads, dst):
+        """Waits for every rank's `epoch` (always launched, also with one
+        rank) and copies heads [head0, head0 + n_heads) of the gathered
+        output into dst [rows, n_heads, head_dim] in the same kernel."""
+        rows, heads_total, D = self.shape
+        check(self.L.s1kv_exchange_wait_copy(self.h, epoch, dst.shape[0], heads_total, D, head0, n_heads, _dptr(dst),
+                                             _stream()))
+        return dst
 
     def output(self, epoch, rows=None):
         """The gathered [rows, heads_total, head_dim] of `epoch` (a view of

@@ -459,6 +459,13 @@ def test_head_sharded_exchange_on_one_gpu(s1kv, oracle, cuda, dtype):
             ref = np.concatenate(pmap(lambda i: ops[layer].attention(seqs[i], q[i:i + 1], Hq), range(B)))
             for r in range(world):
                 worst = max(worst, rel_err(got[r], ref))
+            # the wait fused with a copy of one head range (the other rank's
+            # heads, as the next layer's queries): the same bits as the buffer
+            for r in range(world):
+                h0 = (1 - r) * hq
+                dst = torch.full((B, hq, D), float("nan"), device="cuda")
+                exs[r].wait_copy(epoch, h0, hq, dst)
+                np.testing.assert_array_equal(host(dst), got[r][:, h0:h0 + hq])
     print(f"head-sharded exchange on one GPU ({dtype}): rel err {worst:.2e}")
     assert worst <= TOL_F32, worst
     torch.cuda.synchronize()

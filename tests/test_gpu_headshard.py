@@ -90,7 +90,7 @@ def _rank_fused(rank, world, port, out_dir):
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
     Hq, Hkv, D, bs = 32, 8, 128, 16
-    ctx = [300, 517, 1024]
+    ctx = FUSED_CTX
     B = len(ctx)
     rng = np.random.default_rng(7)
     k = [rng.standard_normal((c, Hkv, D), dtype=np.float32) for c in ctx]
@@ -105,11 +105,15 @@ def _rank_fused(rank, world, port, out_dir):
         b.append(0, torch.from_numpy(np.concatenate([x[:, kv_lo:kv_hi] for x in k])).cuda().contiguous(),
                  torch.from_numpy(np.concatenate([x[:, kv_lo:kv_hi] for x in v])).cuda().contiguous())
     ex = s1kv.PeerExchange(rank, world, B, Hq, D)
-    outs = []
+    outs, slices = [], []
+    hq = q_hi - q_lo
     with pool.batch(seqs, [0] * B, [1] * B) as b:
         for e in (1, 2, 3):  # both slots, and one reused
             ex.attention(b, 0, torch.from_numpy(qs[e - 1][:, q_lo:q_hi].copy()).cuda(), q_lo, e)
-            ex.wait(e)
+            if e == 2:
+                ex.wait(e)
+            else:  # the wait fused with a copy of the other rank's heads
+                slices.append(ex.wait_copy(e, (1 - rank) * hq, hq, torch.empty((B, hq, D), device="cuda")))
             outs.append(ex.output(e).clone())
     torch.cuda.synchronize()
     assert pool.check_device() == 0
@@ -119,14 +123,19 @@ def _rank_fused(rank, world, port, out_dir):
     dist.barrier()
     dist.destroy_process_group()
     np.save(os.path.join(out_dir, f"fused{rank}.npy"), torch.stack(outs).cpu().numpy())
+    np.save(os.path.join(out_dir, f"slices{rank}.npy"), torch.stack(slices).cpu().numpy())
+
+
+FUSED_CTX = [300, 517, 1024, 40000]  # the long row: 63 splits, merged in two levels
 
 
 @pytest.mark.gpu
 def test_two_gpu_fused_exchange_matches_oracle(tmp_path, oracle):
     """The decode kernels of each rank store their heads' rows into both
-    ranks' token-major buffers over NVLink (no NCCL, no reorder): three
-    epochs in a row, each rank's buffer equals the oracle's full-head
-    attention (2e-5 x max |ref|)."""
+    ranks' token-major buffers over NVLink (no NCCL, no reorder), also the
+    rows merged in two levels: three epochs in a row, each rank's buffer
+    equals the oracle's full-head attention (2e-5 x max |ref|), and the
+    waits fused with a copy of the other rank's heads copy them exactly."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -134,17 +143,22 @@ def test_two_gpu_fused_exchange_matches_oracle(tmp_path, oracle):
     world = 2
     mp.start_processes(_rank_fused, args=(world, _port(), str(tmp_path)), nprocs=world, start_method="spawn", join=True)
     Hq, Hkv, D = 32, 8, 128
-    ctx = [300, 517, 1024]
+    ctx = FUSED_CTX
     rng = np.random.default_rng(7)
     k = [rng.standard_normal((c, Hkv, D), dtype=np.float32) for c in ctx]
     v = [rng.standard_normal((c, Hkv, D), dtype=np.float32) for c in ctx]
     qs = rng.standard_normal((3, len(ctx), Hq, D), dtype=np.float32)
+    hq = Hq // world
     for r in range(world):
         got = np.load(tmp_path / f"fused{r}.npy")
+        sl = np.load(tmp_path / f"slices{r}.npy")
         for e in range(3):
             ref = np.stack([oracle.gqa_attention(qs[e][s:s + 1], oracle.bf16_round(k[s]), oracle.bf16_round(v[s]), Hq,
                                                  Hkv, D)[0] for s in range(len(ctx))])
             assert np.max(np.abs(got[e] - ref)) <= 2e-5 * np.max(np.abs(ref))
+        h0 = (1 - r) * hq
+        for i, e in enumerate((0, 2)):  # epochs 1 and 3 copied a head range
+            np.testing.assert_array_equal(sl[i], got[e][:, h0:h0 + hq])
 
 
 @pytest.mark.gpu
