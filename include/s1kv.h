@@ -380,7 +380,13 @@ int s1kv_debug_div_check(const float* xs, int64_t nx, const float* ds, int64_t n
                          void* stream);
 /* Append without RoPE (KVBlockPool::append data movement). */
 int s1kv_batch_append(s1kv_batch* batch, int32_t layer, const float* k, const float* v, void* stream);
-/* Paged GQA attention of the batch's query rows (post-RoPE q). */
+/* Paged GQA attention of the batch's query rows (post-RoPE q).  For decode
+ * batches (at most one query row per sequence) the kernel is a programmatic
+ * dependent launch that may request the K/V of tokens this batch did not
+ * append while the previous kernel of the stream is still running; every
+ * kernel of this library that writes the pool elsewhere completes before a
+ * later kernel starts.  A caller's own programmatic-dependent kernel that
+ * writes the pool must therefore not come directly before this call. */
 int s1kv_batch_attention(s1kv_batch* batch, int32_t layer, const float* q, float* out, int32_t n_q_heads,
                          void* stream);
 /* End-to-end layer step with HOST buffers (pinned for full speed): copies

@@ -110,7 +110,10 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
     std::vector<int64_t> lens(n_seqs);
     std::vector<int32_t> trow(n_seqs);
     int64_t n_tok = 0;
-    for (int32_t i = 0; i < n_seqs; i++) n_tok += n_append ? std::max<int32_t>(n_append[i], 0) : 0;
+    for (int32_t i = 0; i < n_seqs; i++) {
+        n_tok += n_append ? std::max<int32_t>(n_append[i], 0) : 0;
+        b->max_append = std::max<int32_t>(b->max_append, n_append ? n_append[i] : 0);
+    }
     slots.resize(n_tok);
     pos.resize(n_tok);
     int64_t off = 0;
@@ -291,7 +294,7 @@ static int batch_append_impl(s1kv_batch* b, int32_t layer, const float* q_in, fl
         if (st) return st;
     }
     if (b->n_tokens) {
-        st = launch_append(ap, p->desc.dtype, rope, stream);
+        st = launch_append(ap, p->desc.dtype, rope, stream, true);
         if (st) return st;
     }
     if (rope && q_in && !fused_q && b->n_rows)
@@ -405,6 +408,19 @@ static int split_k_attention(s1kv_batch* b, int32_t layer, const float* q, float
     ap.layer = layer;
     ap.scale_log2 = scale_log2(D);
     ap.err = p->d_err;
+    // Decode rows: the kernels request the K/V tiles that lie entirely below
+    // the last max_append tokens of each row before their wait for the
+    // previous kernel of the stream.  Safe because the kernels of this
+    // library that may still run then write the pool only at this batch's
+    // appended tokens (the batch's RoPE + append of any layer; the decode
+    // kernels read it): every other write of the pool -- single-call
+    // appends, copy-on-write copies, block-table updates, prefix loads -- is
+    // a plain launch or a copy, complete before any later kernel starts, and
+    // the step's metadata is uploaded before the batch's first kernel.
+    if (b->decode_rows) {
+        ap.prewait = 1;
+        ap.prewait_margin = b->max_append;
+    }
     const size_t cbytes = (size_t)b->n_rows * Hkv * kCounterStride * sizeof(int32_t);
     if (p->counters.cap < cbytes) {
         st = p->counters.ensure(cbytes);
@@ -579,7 +595,7 @@ int s1kv_append(s1kv_pool* p, int32_t layer, const float* k, const float* v, con
     ap.Hkv = p->desc.num_kv_heads;
     ap.D = p->desc.head_dim;
     ap.err = p->d_err;
-    return launch_append(ap, p->desc.dtype, false, (cudaStream_t)stream);
+    return launch_append(ap, p->desc.dtype, false, (cudaStream_t)stream, false);
 }
 
 int s1kv_rope_append(s1kv_pool* p, int32_t layer, const float* q_in, float* q_out, int32_t Hq, const float* k,
@@ -615,7 +631,7 @@ int s1kv_rope_append(s1kv_pool* p, int32_t layer, const float* q_in, float* q_ou
     ap.rope = rope_table(p->device, p->desc.head_dim, p->desc.rope_theta, bound, &ap.rope_cap, (cudaStream_t)stream,
                          &st);
     if (st) return st;
-    return launch_append(ap, p->desc.dtype, true, (cudaStream_t)stream);
+    return launch_append(ap, p->desc.dtype, true, (cudaStream_t)stream, false);
 }
 
 int s1kv_apply_rope(const float* x, float* out, int64_t start_pos, int64_t n, int32_t H, int32_t D, float theta,

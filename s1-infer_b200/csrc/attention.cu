@@ -241,7 +241,9 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, 
     constexpr int NW = C::kNW, NS = C::kNS, NV = C::kNV, LPT = C::kLPT, IT = C::kIT, EPC = C::kEPC,
                   TPS = C::kTPS, STEPS = C::kSteps, DPL = C::kDPL, DQ = C::kDQ, TILE = C::kTile;
     extern __shared__ __align__(1024) uint8_t smem[];
-    pdl_enter();
+    // The next kernel may launch now; this one waits for the previous kernel
+    // (griddepcontrol.wait) before it reads anything that kernel may write.
+    pdl_trigger();
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // CTA index = item * Hkv + head: the heads of one item run side by side
@@ -286,8 +288,22 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, 
         tma_load_4d(dst + C::kTileBytes, &tmV, &bar[s], 0, h, row, p.layer);
     };
     {
-        const int pre = min(NS, my_tiles);
+        // The first copies: tiles entirely below the tokens this batch
+        // appends are requested before the wait (items, block table and those
+        // K/V rows were written before the previous kernel started), the
+        // rest after it.
+        const int n_first = min(NS, my_tiles);
+        int pre = 0;
+        if (p.prewait) {
+            const int safe_end = item.kv_len - p.prewait_margin;
+            while (pre < n_first && tok0 + (warp + pre * NW) * TILE + TILE <= safe_end) pre++;
+        }
         for (int k = 0; k < pre; k++) {
+            const int row = __shfl_sync(kFull, my_row, k);
+            if (lane == 0) issue(k, row);
+        }
+        pdl_wait();
+        for (int k = pre; k < n_first; k++) {
             const int row = __shfl_sync(kFull, my_row, k);
             if (lane == 0) issue(k, row);
         }

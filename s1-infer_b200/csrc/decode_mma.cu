@@ -143,7 +143,9 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
                       const __grid_constant__ CUtensorMap tmV) {
     static_assert(G >= 1 && G <= 8, "query heads per KV head must fit the 8 live rows of an m16 tile");
     extern __shared__ uint8_t smem_raw[];
-    pdl_enter();
+    // The next kernel may launch now; this one waits for the previous kernel
+    // (griddepcontrol.wait) before it reads anything that kernel may write.
+    pdl_trigger();
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;  // mma fragment coordinates: head row, column pair
@@ -184,7 +186,21 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
         tma5(dst, &tmK, &bar[s], 0, row, 0, h, p.layer);  // both halves of the block's 16 rows
         tma5(dst + kTileBytes, &tmV, &bar[s], 0, row, 0, h, p.layer);
     };
-    for (int k = 0; k < min(kNS, my_tiles); k++) {
+    // The first copies: tiles entirely below the tokens this batch appends
+    // are requested before the wait (items, block table and those K/V rows
+    // were written before the previous kernel started), the rest after it.
+    const int n_first = min(kNS, my_tiles);
+    int pre = 0;
+    if (p.prewait) {
+        const int safe_end = item.kv_len - p.prewait_margin;
+        while (pre < n_first && tok0 + (warp + pre * kNW) * kTile + kTile <= safe_end) pre++;
+    }
+    for (int k = 0; k < pre; k++) {
+        const int row = __shfl_sync(kFull, my_row, k);
+        if (lane == 0) issue(k, row);
+    }
+    pdl_wait();
+    for (int k = pre; k < n_first; k++) {
         const int row = __shfl_sync(kFull, my_row, k);
         if (lane == 0) issue(k, row);
     }

@@ -89,6 +89,8 @@ __device__ __forceinline__ void pdl_enter() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
 }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 #endif
 
 #define S1KV_ON_DEVICE(dev)                                            \
@@ -168,6 +170,13 @@ struct AttnParams {
     int32_t n_flags;
     uint32_t* flag_dst[8]; // this rank's flag on every rank (self included)
     uint32_t epoch;
+    // Copies issued before the wait for the previous kernel (decode rows of
+    // a batch): when prewait is set, a tile whose tokens all lie below
+    // kv_len - prewait_margin (the tokens appended by this batch are the
+    // last prewait_margin of each sequence) is requested before
+    // griddepcontrol.wait.  See split_k_attention for why that is safe.
+    int32_t prewait;
+    int32_t prewait_margin;
 };
 
 // One sequence of a prefill batch (tensor-core prefill kernel).
@@ -349,6 +358,7 @@ struct s1kv_batch {
     int64_t max_pos = 0;      // largest position appended + 1
     bool decode_rows = true;  // every row has q_len 1 for its sequence
     bool rows_are_tokens = true;  // q_len == n_append for every sequence: query row i is appended token i
+    int32_t max_append = 0;   // the most tokens any sequence appends in this batch
     const int32_t* d_qpos = nullptr;  // position of each query row (kv_len - 1), when rows are not the tokens
     // device views into seg->d
     const int32_t* d_slots = nullptr;
@@ -370,7 +380,10 @@ namespace s1kv {
 // --------------------------------------------------------------- kernels --
 int launch_table_update(const TableUpdate* d_upd, int64_t n, int32_t* table, int32_t max_bps, cudaStream_t stream);
 int launch_cow(s1kv_pool* pool, const int32_t* d_src, const int32_t* d_dst, int64_t n, cudaStream_t stream);
-int launch_append(const AppendParams& p, int dtype, bool rope, cudaStream_t stream);
+// pdl: launched as a programmatic dependent launch (the batch's appends);
+// the single-call entry points launch plainly, so that a kernel after them
+// never starts before their writes are complete.
+int launch_append(const AppendParams& p, int dtype, bool rope, cudaStream_t stream, bool pdl);
 // q/k RMSNorm + RoPE + append (k, v to slots; q rows at qpos to q_out).
 int launch_norm_rope_append(const AppendParams& p, int dtype, const float* qw, const float* kw, float eps,
                             const int32_t* qpos, int64_t n_q_rows, cudaStream_t stream);

@@ -244,7 +244,7 @@ __global__ void append_scalar_kernel(const AppendParams p) {
 
 static bool aligned16(const void* ptr) { return ((uintptr_t)ptr & 15) == 0; }
 
-int launch_append(const AppendParams& p, int dtype, bool rope, cudaStream_t stream) {
+int launch_append(const AppendParams& p, int dtype, bool rope, cudaStream_t stream, bool pdl) {
     if (p.n <= 0) return S1KV_OK;
     if (rope && (p.D % 2)) return set_error(S1KV_EINVAL, "RoPE needs an even head_dim");
     bool vec = (p.D % 16 == 0) && aligned16(p.k) && aligned16(p.v) && (!p.q_in || (aligned16(p.q_in) && aligned16(p.q_out)));
@@ -252,8 +252,15 @@ int launch_append(const AppendParams& p, int dtype, bool rope, cudaStream_t stre
                         : (2 * p.n * p.Hkv + (rope && p.q_in ? p.n * p.Hq : 0)) * p.D;
     int grid = (int)std::max<int64_t>(1, std::min<int64_t>((units + 255) / 256, kSMs * 16));
 #define S1KV_APPEND(T, R)                                                                                    \
-    S1KV_CUDA(vec ? launch_pdl(append_vec_kernel<T, R>, dim3(grid), dim3(256), 0, stream, p)                    \
-                  : launch_pdl(append_scalar_kernel<T, R>, dim3(grid), dim3(256), 0, stream, p))
+    do {                                                                                                     \
+        if (pdl)                                                                                             \
+            S1KV_CUDA(vec ? launch_pdl(append_vec_kernel<T, R>, dim3(grid), dim3(256), 0, stream, p)            \
+                          : launch_pdl(append_scalar_kernel<T, R>, dim3(grid), dim3(256), 0, stream, p));       \
+        else if (vec)                                                                                        \
+            append_vec_kernel<T, R><<<grid, 256, 0, stream>>>(p);                                            \
+        else                                                                                                 \
+            append_scalar_kernel<T, R><<<grid, 256, 0, stream>>>(p);                                         \
+    } while (0)
     if (dtype == S1KV_DTYPE_F32) {
         if (rope) S1KV_APPEND(float, true);
         else S1KV_APPEND(float, false);
