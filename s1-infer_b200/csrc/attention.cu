@@ -241,9 +241,6 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, 
     constexpr int NW = C::kNW, NS = C::kNS, NV = C::kNV, LPT = C::kLPT, IT = C::kIT, EPC = C::kEPC,
                   TPS = C::kTPS, STEPS = C::kSteps, DPL = C::kDPL, DQ = C::kDQ, TILE = C::kTile;
     extern __shared__ __align__(1024) uint8_t smem[];
-    // The next kernel may launch now; this one waits for the previous kernel
-    // (griddepcontrol.wait) before it reads anything that kernel may write.
-    pdl_trigger();
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // CTA index = item * Hkv + head: the heads of one item run side by side
@@ -434,6 +431,13 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, 
         }
     }
 
+    // The next kernel of the stream may launch once every CTA got here: its
+    // CTAs then take the slots this launch frees as it ends (and overlap the
+    // merge of the splits) instead of slots beside CTAs still streaming K/V,
+    // which skews the next launch's CTAs over the SMs.  This kernel waits
+    // for the previous one (griddepcontrol.wait) before reading what it
+    // writes.
+    pdl_trigger();
     if (failed) {
         // Drain this warp's copies still in flight before the CTA exits.
         if (lane == 0) atomicOr(p.err, kErrTimeout);

@@ -143,9 +143,6 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
                       const __grid_constant__ CUtensorMap tmV) {
     static_assert(G >= 1 && G <= 8, "query heads per KV head must fit the 8 live rows of an m16 tile");
     extern __shared__ uint8_t smem_raw[];
-    // The next kernel may launch now; this one waits for the previous kernel
-    // (griddepcontrol.wait) before it reads anything that kernel may write.
-    pdl_trigger();
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;  // mma fragment coordinates: head row, column pair
@@ -332,6 +329,13 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
         }
     }
 
+    // The next kernel of the stream may launch once every CTA got here: its
+    // CTAs then take the slots this launch frees as it ends (and overlap the
+    // merge of the splits) instead of slots beside CTAs still streaming K/V,
+    // which skews the next launch's CTAs over the SMs.  This kernel waits
+    // for the previous one (griddepcontrol.wait) before reading what it
+    // writes.
+    pdl_trigger();
     if (failed) {
         // drain this warp's copies still in flight before the CTA exits
         if (lane == 0) atomicOr(p.err, kErrTimeout);
