@@ -528,7 +528,12 @@ def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3, shard=None, max_layer
     gbuf = torch.empty((world, B, hq, D), device="cuda")
     nxt = (rank + 1) % world
 
-    ex = s1kv.PeerExchange(rank, world, B, hq_all, D)
+    # one process standing in for one rank of `shard`: no other rank writes
+    # the other heads, so its exchange holds its own heads only (the wait
+    # checks every word of the slot)
+    ex_heads = hq if world == 1 and (shard or 1) > 1 else hq_all
+    ex_h0, ex_nxt = (q_lo, nxt * hq) if ex_heads == hq_all else (0, 0)
+    ex = s1kv.PeerExchange(rank, world, B, ex_heads, D)
     epoch = [0]
 
     def step(ev=None, fused=False):
@@ -546,10 +551,10 @@ def run_cfg4(s1kv, torch, rank, world, steps=10, warmup=3, shard=None, max_layer
                     # one kernel waits for every rank and copies the next
                     # layer's query heads out
                     epoch[0] += 1
-                    ex.attention(bt, layer, q_rot, q_lo, epoch[0])
+                    ex.attention(bt, layer, q_rot, ex_h0, epoch[0])
                     if ev is not None:
                         ev[layer][1].record()
-                    q = ex.wait_copy(epoch[0], nxt * hq, hq, q_next)
+                    q = ex.wait_copy(epoch[0], ex_nxt, hq, q_next)
                 else:
                     bt.attention(layer, q_rot, out=out)
                     if ev is not None:

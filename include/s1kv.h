@@ -213,17 +213,24 @@ int s1kv_prefix_load_v1(s1kv_pool* pool, uint64_t seq, const char* path, int32_t
 /* No reference counterpart (s1-infer is single-process).  One process per
  * GPU; rank r keeps KV heads [r*Hkv/N, (r+1)*Hkv/N) and their query heads.
  * Each rank creates an exchange holding two layer slots of the token-major
- * output [rows][all query heads][head_dim] (fp32, slot_floats floats each;
+ * output [rows][all query heads][head_dim] (slot_floats elements each;
  * layers alternate by epoch parity), exports its CUDA IPC handle (64 bytes),
  * and opens every peer's from the array of all ranks' handles (world x 64
- * bytes, in rank order).  s1kv_batch_attention_exchange runs a decode
- * batch's attention for this rank's heads and stores each finished row into
- * its place in every rank's slot over NVLink, then signals `epoch`;
- * s1kv_exchange_wait (device, bounded: sets the timeout bit of the error word
- * after about a second) makes the stream wait until all ranks signalled it;
- * it is a programmatic dependent launch, resident while this rank's decode
- * kernel finishes, and polls only after that kernel completed.
- * Epochs increase by one per layer step. */
+ * bytes, in rank order).  An element is one 64-bit word: the epoch that
+ * wrote it in the high 32 bits, the fp32 value's bits in the low 32.
+ * s1kv_batch_attention_exchange runs a decode batch's attention for this
+ * rank's heads and stores each finished element, tagged with `epoch`, into
+ * its place in every rank's slot over NVLink (no fence or flag: a 64-bit
+ * store is seen whole or not at all); s1kv_exchange_wait (device, bounded:
+ * sets the timeout bit of the error word after about a second) makes the
+ * stream wait until every word that the epoch's attention fills, on all
+ * ranks, carries the epoch; it is a programmatic dependent launch, resident
+ * while this rank's decode kernel finishes, and polls only after that
+ * kernel completed.  Epochs start at 1 and increase by one per layer step;
+ * every rank waits for each epoch (s1kv_exchange_wait or _wait_copy) on the
+ * stream of its attention before its attention of the next epoch -- that
+ * wait on all ranks' words is what makes reusing a slot two epochs later
+ * safe. */
 typedef struct s1kv_exchange s1kv_exchange;
 int s1kv_exchange_create(int device, int32_t rank, int32_t world, int64_t slot_floats, s1kv_exchange** out);
 int s1kv_exchange_handle(const s1kv_exchange* ex, void* handle64);
@@ -235,16 +242,20 @@ int s1kv_exchange_open(s1kv_exchange* ex, const void* handles);
  * Replaces the IPC handle exchange of s1kv_exchange_open. */
 void* s1kv_exchange_base(const s1kv_exchange* ex);
 int s1kv_exchange_open_local(s1kv_exchange* ex, void* const* bases);
-/* Device address of the slot `epoch` uses: [rows][heads_total][head_dim]. */
-float* s1kv_exchange_buffer(const s1kv_exchange* ex, uint32_t epoch);
+/* Device address of the slot `epoch` uses: [rows][heads_total][head_dim]
+ * 64-bit words (epoch << 32 | float bits; on a little-endian GPU the float
+ * is the first 4 bytes of each word). */
+void* s1kv_exchange_buffer(const s1kv_exchange* ex, uint32_t epoch);
+/* Waits for the words this rank's s1kv_batch_attention_exchange of `epoch`
+ * filled (the whole slot if it issued none). */
 int s1kv_exchange_wait(s1kv_exchange* ex, uint32_t epoch, void* stream);
 /* s1kv_exchange_wait, then (in the same kernel) a copy of heads [head0,
  * head0 + n_heads) of every row of the epoch's slot, laid out [rows]
- * [heads_total][head_dim] as s1kv_batch_attention_exchange wrote it, into
- * dst [rows][n_heads][head_dim] (device, 16-byte aligned; head_dim a
- * multiple of 4).  For a consumer that wants one contiguous head range of
- * the gathered output, e.g. the query heads a rank feeds to its next layer.
- * On a timeout dst is left unwritten (and the timeout bit set). */
+ * [heads_total][head_dim] as s1kv_batch_attention_exchange wrote it (rows x
+ * heads_total x head_dim equal to what it wrote), into dst [rows][n_heads]
+ * [head_dim] fp32 (device).  For a consumer that wants one contiguous head
+ * range of the gathered output, e.g. the query heads a rank feeds to its
+ * next layer.  On a timeout dst is incomplete (and the timeout bit set). */
 int s1kv_exchange_wait_copy(s1kv_exchange* ex, uint32_t epoch, int32_t rows, int32_t heads_total, int32_t head_dim,
                             int32_t head0, int32_t n_heads, float* dst, void* stream);
 int s1kv_exchange_destroy(s1kv_exchange* ex);

@@ -432,11 +432,8 @@ static int split_k_attention(s1kv_batch* b, int32_t layer, const float* q, float
         ap.out_stride = ex->out_stride;
         ap.out_head0 = ex->out_head0;
         ap.n_peers = ex->n_peers;
-        for (int k = 0; k < 7; k++) ap.peer_out[k] = ex->peer_out[k];
-        ap.done = ex->done;
-        ap.done_total = (int32_t)(b->n_rows * Hkv);
-        ap.n_flags = ex->n_flags;
-        for (int k = 0; k < 8; k++) ap.flag_dst[k] = ex->flag_dst[k];
+        ap.xout = ex->xout;
+        for (int k = 0; k < 7; k++) ap.xpeer[k] = ex->xpeer[k];
         ap.epoch = ex->epoch;
     }
     return launch_attention(p, ap, p->desc.dtype, stream);
@@ -500,11 +497,13 @@ int s1kv_batch_attention_exchange(s1kv_batch* b, int32_t layer, const float* q, 
         return set_error(S1KV_EINVAL, "exchange: shape not served by the split-K decode kernels");
     if (head0 < 0 || head0 + Hq > heads_total || (int64_t)b->n_rows * heads_total * D > ex->slot_floats)
         return set_error(S1KV_EINVAL, "exchange: rows x heads x head_dim exceed the exchange slot");
+    if (epoch == 0) return set_error(S1KV_EINVAL, "exchange: epochs start at 1 (0 is the zeroed slot's)");
     AttnParams ex_p{};
     st = exchange_params(ex, epoch, head0, heads_total, &ex_p);
     if (st) return st;
+    exchange_record(ex, epoch, (int64_t)b->n_rows * heads_total * D);
     if (b->n_rows == 0) return S1KV_OK;
-    return split_k_attention(b, layer, q, ex_p.out, Hq, &ex_p, (cudaStream_t)stream_);
+    return split_k_attention(b, layer, q, nullptr, Hq, &ex_p, (cudaStream_t)stream_);
 }
 
 int s1kv_batch_layer_host(s1kv_batch* b, int32_t layer, const float* h_q, const float* h_k, const float* h_v,

@@ -494,7 +494,6 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kNW * 32, DecodeCfg<T, D, 
             }
         }
     }
-    if (rm.n_split == 1) signal_done(p);
     if (p.counters && rm.n_split > 1)
         finish_split_row(p, item.row, h, item.split, rm.n_split, G, D,
                          reinterpret_cast<int*>(smem + C::kRing + NW * C::kPFloats * 4 + NW * NS * 8),

@@ -6,31 +6,21 @@
 
 namespace s1kv {
 
-// Stores element d of (row, local head `head`) of the attention output, and
-// the same element of every peer's buffer (NVLink stores).
+// Stores element d of (row, local head `head`) of the attention output.
+// Exchange launches store it into this rank's slot and every peer's (NVLink)
+// as one 64-bit word carrying the epoch beside the value: a single store of
+// aligned 64 bits is seen whole or not at all, so a reader that polls the
+// word until its epoch matches needs no fence, flag or counter from the
+// writer (system scope: the readers run on other GPUs).
 __device__ __forceinline__ void store_out(const AttnParams& p, int64_t row, int head, int d, int D, float v) {
     const int64_t i = (row * (p.out_stride > 0 ? p.out_stride : p.Hq) + p.out_head0 + head) * D + d;
-    p.out[i] = v;
-    for (int k = 0; k < p.n_peers; k++) p.peer_out[k][i] = v;
-}
-
-// Called by every thread of a CTA that has just stored a finished (row, KV
-// head): when the launch's last such CTA arrives, this rank's flag on every
-// rank is set to the epoch (release, system scope), after every store of the
-// launch.  The barrier orders the CTA's stores before thread 0's system-scope
-// fence, which is cumulative over them (the pattern of a grid barrier).
-__device__ __forceinline__ void signal_done(const AttnParams& p) {
-    if (!p.done) return;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        const uint32_t prev = atomicAdd(p.done, 1u);
-        if (prev == (uint32_t)p.done_total - 1) {
-            *p.done = 0;
-            __threadfence_system();
-            for (int r = 0; r < p.n_flags; r++)
-                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.flag_dst[r]), "r"(p.epoch) : "memory");
-        }
+    if (p.xout) {
+        const uint64_t w = ((uint64_t)p.epoch << 32) | __float_as_uint(v);
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p.xout + i), "l"(w) : "memory");
+        for (int k = 0; k < p.n_peers; k++)
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p.xpeer[k] + i), "l"(w) : "memory");
+    } else {
+        p.out[i] = v;
     }
 }
 
@@ -211,7 +201,6 @@ __device__ __forceinline__ void finish_split_row(const AttnParams& p, int row, i
             merge_staged(p, row, h, G, D, scratch, 0, n_split, 1, false, 0);
         else
             combine_partials(p, row, h, G, D, threadIdx.x, blockDim.x);
-        signal_done(p);
         return;
     }
     const int grp = split / kMergeGroup, n_groups = (n_split + kMergeGroup - 1) / kMergeGroup;
@@ -220,7 +209,6 @@ __device__ __forceinline__ void finish_split_row(const AttnParams& p, int row, i
     merge_staged(p, row, h, G, D, scratch, first, in_grp, 1, true, first);
     if (!arrive_last(ctr, n_groups, flag)) return;
     merge_staged(p, row, h, G, D, scratch, 0, n_groups, kMergeGroup, false, 0);
-    signal_done(p);
 }
 
 }  // namespace s1kv

@@ -405,7 +405,6 @@ __global__ void __launch_bounds__(kNW * 32, kMinCtas)
             }
         }
     }
-    if (rm.n_split == 1) signal_done(p);
     if (p.counters && rm.n_split > 1)
         finish_split_row(p, item.row, h, item.split, rm.n_split, G, kD, reinterpret_cast<int*>(smem + kRing + kNW * kNS * 8),
                          reinterpret_cast<float*>(smem), kRing / 4);  // the rings are free by now

@@ -3,16 +3,18 @@
 // thread).
 //
 // Every rank owns one device allocation: two layer slots of the token-major
-// output [rows][all query heads][head_dim] (fp32; layers alternate slots),
-// then flags[2][8] (uint32, the epoch rank r last finished in that slot),
-// then one completion counter.  The allocation is shared with the other
-// ranks' processes through CUDA IPC handles; the decode kernels store every
-// finished row into its place in all ranks' slot (NVLink stores), and the
-// launch's last CTA sets this rank's flag on every rank (release, system
-// scope).  Before reading a slot, a rank waits (bounded) until every rank's
-// flag reached the epoch.  Reuse of a slot two layers later is safe: no rank
-// can reach it before every rank has finished the layer in between, which
-// needs this slot's contents.
+// output [rows][all query heads][head_dim], one 64-bit word per element
+// (epoch << 32 | float bits; layers alternate slots by epoch parity).  The
+// allocation is shared with the other ranks' processes through CUDA IPC
+// handles; the decode kernels store every finished element into its place
+// in all ranks' slot (NVLink stores of whole words).  A reader polls the
+// words themselves until each carries the epoch: no fence, flag or counter
+// on the writer's side, and a word is never seen half written.  Reuse of a
+// slot two layers later is safe because every wait checks the words of ALL
+// ranks: no rank writes epoch e + 2 before it has waited for epoch e + 1,
+// which every rank writes only after its own wait for epoch e, i.e. after
+// it read the slot.
+#include <algorithm>
 #include <cstring>
 
 #include "internal.h"
@@ -20,45 +22,55 @@
 namespace s1kv {
 namespace {
 
-constexpr uint32_t kWaitSpins = 1u << 24;  // about a second with the back-off below
+constexpr uint32_t kWaitSpins = 1u << 24;  // per thread: about a second with the back-off below
+constexpr int kWaitThreads = 256;
+constexpr int kWaitPer = 4;                 // words per thread per pass, loads in flight together
 
-size_t flags_offset(int64_t slot_floats) { return (size_t)2 * slot_floats * sizeof(float); }
-size_t done_offset(int64_t slot_floats) { return flags_offset(slot_floats) + 2 * 8 * sizeof(uint32_t); }
-size_t alloc_bytes(int64_t slot_floats) { return done_offset(slot_floats) + 256; }
+size_t alloc_bytes(int64_t slot_floats) { return (size_t)2 * slot_floats * sizeof(uint64_t); }
 
-// Lane r of warp 0 waits until rank r's flag in this slot has reached
-// `epoch`; then, when `dst` is set, the CTA copies heads [head0, head0 +
-// n_heads) of every row of the slot [rows][heads_total][D] into dst [rows]
-// [n_heads][D].  Launched as a programmatic dependent launch: the CTA may
-// become resident while this rank's decode kernel still runs, and waits for
-// it to complete (griddepcontrol.wait) before polling, so the only waits
-// left are on the other GPUs' kernels.
-__global__ void exchange_wait_kernel(const uint32_t* flags, int world, uint32_t epoch, int* err, const float* slot,
-                                     int rows, int heads_total, int D, int head0, int n_heads, float* dst) {
+// Polls words [0, words) of a slot until each carries `epoch`; when dst is
+// set, the words of heads [head0, head0 + n_heads) go to dst [rows]
+// [n_heads][D] as floats.  A thread gives up after kWaitSpins polls in all
+// and sets the timeout bit (dst is then incomplete).  Launched as a
+// programmatic dependent launch: the CTAs may become resident while this
+// rank's decode kernel still runs and wait for it to complete
+// (griddepcontrol.wait), so the only waits left are on the other GPUs'.
+__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+__global__ void exchange_wait_kernel(const uint64_t* slot, int64_t words, uint32_t epoch, int* err, int heads_total,
+                                     int D, int head0, int n_heads, float* dst) {
     pdl_enter();
-    __shared__ int ok;
-    if (threadIdx.x < 32) {
-        const int r = threadIdx.x;
-        bool seen = r >= world;
-        for (uint32_t i = 0; i < kWaitSpins && !seen; i++) {
-            uint32_t v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
-            seen = (int32_t)(v - epoch) >= 0;
-            if (!seen) __nanosleep(64);
+    uint32_t spins = 0;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < words; i0 += kWaitPer * stride) {
+        // the pass's words are requested together (one round trip), then each
+        // is polled again until its epoch matches
+        uint64_t w[kWaitPer];
+#pragma unroll
+        for (int u = 0; u < kWaitPer; u++) w[u] = i0 + u * stride < words ? ld_word(slot + i0 + u * stride) : 0;
+#pragma unroll
+        for (int u = 0; u < kWaitPer; u++) {
+            const int64_t i = i0 + u * stride;
+            if (i >= words) break;
+            while ((uint32_t)(w[u] >> 32) != epoch) {
+                if (++spins >= kWaitSpins) {
+                    atomicOr(err, kErrTimeout);
+                    return;
+                }
+                __nanosleep(64);
+                w[u] = ld_word(slot + i);
+            }
+            if (dst) {
+                const int64_t rh = i / D;
+                const int hh = (int)(rh % heads_total) - head0;
+                if (hh >= 0 && hh < n_heads)
+                    dst[((rh / heads_total) * n_heads + hh) * D + i % D] = __uint_as_float((uint32_t)w[u]);
+            }
         }
-        const bool all = __all_sync(0xffffffffu, seen);
-        if (threadIdx.x == 0) {
-            if (!all) atomicOr(err, kErrTimeout);
-            ok = all;
-        }
-    }
-    __syncthreads();
-    if (!dst || !ok) return;
-    const int per_row = n_heads * D / 4;  // float4 per row
-    for (int i = threadIdx.x; i < rows * per_row; i += blockDim.x) {
-        const int row = i / per_row, c = i % per_row;
-        reinterpret_cast<float4*>(dst)[i] =
-            reinterpret_cast<const float4*>(slot + ((int64_t)row * heads_total + head0) * D)[c];
     }
 }
 
@@ -67,20 +79,22 @@ __global__ void exchange_wait_kernel(const uint32_t* flags, int world, uint32_t 
 // Fills the exchange fields of `ap` for a launch writing `epoch`'s slot.
 int exchange_params(const s1kv_exchange* ex, uint32_t epoch, int32_t head0, int32_t heads_total, AttnParams* ap) {
     if (!ex->opened && ex->world > 1) return set_error(S1KV_EINVAL, "exchange: peers not opened");
-    const int s = epoch & 1;
-    ap->out = reinterpret_cast<float*>(ex->base + (size_t)s * ex->slot_floats * sizeof(float));
+    const size_t off = (size_t)(epoch & 1) * ex->slot_floats * sizeof(uint64_t);
+    ap->xout = reinterpret_cast<uint64_t*>(ex->base + off);
     ap->out_stride = heads_total;
     ap->out_head0 = head0;
     ap->n_peers = 0;
-    for (int q = 0; q < ex->world; q++) {
-        char* b = q == ex->rank ? ex->base : ex->peer_base[q];
-        if (q != ex->rank) ap->peer_out[ap->n_peers++] = reinterpret_cast<float*>(b + (size_t)s * ex->slot_floats * sizeof(float));
-        ap->flag_dst[q] = reinterpret_cast<uint32_t*>(b + flags_offset(ex->slot_floats)) + s * 8 + ex->rank;
-    }
-    ap->n_flags = ex->world;
-    ap->done = reinterpret_cast<uint32_t*>(ex->base + done_offset(ex->slot_floats));
+    for (int q = 0; q < ex->world; q++)
+        if (q != ex->rank) ap->xpeer[ap->n_peers++] = reinterpret_cast<uint64_t*>(ex->peer_base[q] + off);
     ap->epoch = epoch;
     return S1KV_OK;
+}
+
+// The words of the slot that `epoch`'s attention fills (rows x heads x D of
+// the batch; every rank runs the same shape).
+void exchange_record(s1kv_exchange* ex, uint32_t epoch, int64_t words) {
+    ex->used[epoch & 1] = words;
+    ex->used_epoch[epoch & 1] = epoch;
 }
 
 }  // namespace s1kv
@@ -169,36 +183,42 @@ int s1kv_exchange_open_local(s1kv_exchange* ex, void* const* bases) {
     return S1KV_OK;
 }
 
-float* s1kv_exchange_buffer(const s1kv_exchange* ex, uint32_t epoch) {
+void* s1kv_exchange_buffer(const s1kv_exchange* ex, uint32_t epoch) {
     if (!ex) return nullptr;
-    return reinterpret_cast<float*>(ex->base + (size_t)(epoch & 1) * ex->slot_floats * sizeof(float));
+    return ex->base + (size_t)(epoch & 1) * ex->slot_floats * sizeof(uint64_t);
 }
 
-static int exchange_wait_impl(s1kv_exchange* ex, uint32_t epoch, int32_t rows, int32_t heads_total, int32_t head_dim,
+static int exchange_wait_impl(s1kv_exchange* ex, uint32_t epoch, int64_t words, int32_t heads_total, int32_t head_dim,
                               int32_t head0, int32_t n_heads, float* dst, void* stream) {
-    if (!ex) return set_error(S1KV_EINVAL, "null exchange");
     S1KV_ON_DEVICE(ex->device);
-    const uint32_t* flags = reinterpret_cast<const uint32_t*>(ex->base + flags_offset(ex->slot_floats)) + (epoch & 1) * 8;
-    const float* slot = reinterpret_cast<const float*>(ex->base + (size_t)(epoch & 1) * ex->slot_floats * sizeof(float));
-    S1KV_CUDA(launch_pdl(exchange_wait_kernel, dim3(1), dim3(dst ? 256 : 32), 0, (cudaStream_t)stream, flags, ex->world,
-                         epoch, ex->d_err, slot, rows, heads_total, head_dim, head0, n_heads, dst));
+    if (words <= 0) return S1KV_OK;
+    const uint64_t* slot = static_cast<const uint64_t*>(s1kv_exchange_buffer(ex, epoch));
+    const int64_t per_cta = (int64_t)kWaitThreads * kWaitPer;
+    const int blocks = (int)std::min<int64_t>(4 * 148, (words + per_cta - 1) / per_cta);
+    S1KV_CUDA(launch_pdl(exchange_wait_kernel, dim3(blocks), dim3(kWaitThreads), 0, (cudaStream_t)stream, slot, words, epoch,
+                         ex->d_err, heads_total, head_dim, head0, n_heads, dst));
     g_launches++;
     S1KV_CUDA(cudaGetLastError());
     return S1KV_OK;
 }
 
 int s1kv_exchange_wait(s1kv_exchange* ex, uint32_t epoch, void* stream) {
-    return exchange_wait_impl(ex, epoch, 0, 0, 0, 0, 0, nullptr, stream);
+    if (!ex || epoch == 0) return set_error(S1KV_EINVAL, "s1kv_exchange_wait: null exchange or epoch 0");
+    // the words this rank's attention for the epoch filled; without one, the
+    // whole slot
+    const int64_t words = ex->used_epoch[epoch & 1] == epoch ? ex->used[epoch & 1] : ex->slot_floats;
+    return exchange_wait_impl(ex, epoch, words, 1, 1, 0, 0, nullptr, stream);
 }
 
 int s1kv_exchange_wait_copy(s1kv_exchange* ex, uint32_t epoch, int32_t rows, int32_t heads_total, int32_t head_dim,
                             int32_t head0, int32_t n_heads, float* dst, void* stream) {
-    if (!ex || !dst || rows < 0 || heads_total <= 0 || head_dim <= 0 || head0 < 0 || n_heads <= 0 ||
-        head0 + n_heads > heads_total || (n_heads * head_dim) % 4 || head_dim % 4 ||
-        (int64_t)rows * heads_total * head_dim > ex->slot_floats || ((uintptr_t)dst & 15))
-        return set_error(S1KV_EINVAL, "s1kv_exchange_wait_copy: bad shape (head_dim a multiple of 4, dst 16-byte "
-                                      "aligned, rows x heads_total x head_dim within the slot)");
-    return exchange_wait_impl(ex, epoch, rows, heads_total, head_dim, head0, n_heads, dst, stream);
+    const int64_t words = (int64_t)rows * heads_total * head_dim;
+    if (!ex || !dst || epoch == 0 || rows < 0 || heads_total <= 0 || head_dim <= 0 || head0 < 0 || n_heads <= 0 ||
+        head0 + n_heads > heads_total || words > ex->slot_floats ||
+        (ex->used_epoch[epoch & 1] == epoch && ex->used[epoch & 1] != words))
+        return set_error(S1KV_EINVAL, "s1kv_exchange_wait_copy: bad shape (rows x heads_total x head_dim within the "
+                                      "slot and equal to what the epoch's attention wrote; epochs start at 1)");
+    return exchange_wait_impl(ex, epoch, words, heads_total, head_dim, head0, n_heads, dst, stream);
 }
 
 int s1kv_exchange_destroy(s1kv_exchange* ex) {

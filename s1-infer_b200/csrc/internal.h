@@ -159,16 +159,14 @@ struct AttnParams {
     int32_t* counters;     // [n_rows][Hkv][kCounterStride] arrivals of split CTAs, zero between launches;
                            // NULL = partials are merged by a separate combine launch
     // Output placement and the optional exchange of finished rows with peer
-    // GPUs (KV-head sharding): row r, local head j goes to
-    // out[(r * out_stride + out_head0 + j) * D + d] (out_stride 0 = Hq) and
-    // the same element of every peer_out buffer.
+    // GPUs (KV-head sharding): row r, local head j is element
+    // (r * out_stride + out_head0 + j) * D + d (out_stride 0 = Hq) of out,
+    // or, when xout is set, of xout and of every xpeer buffer as one 64-bit
+    // word (epoch << 32 | float bits) that a reader polls.
     int32_t out_stride, out_head0;
     int32_t n_peers;
-    float* peer_out[7];
-    uint32_t* done;        // completion count of this launch's finished rows (NULL: no signal)
-    int32_t done_total;    // rows x KV heads
-    int32_t n_flags;
-    uint32_t* flag_dst[8]; // this rank's flag on every rank (self included)
+    uint64_t* xout;
+    uint64_t* xpeer[7];
     uint32_t epoch;
     // Copies issued before the wait for the previous kernel (decode rows of
     // a batch): when prewait is set, a tile whose tokens all lie below
@@ -339,8 +337,10 @@ struct s1kv_pool {
 // Peer exchange of attention outputs for KV-head sharding (exchange.cu).
 struct s1kv_exchange {
     int device = 0, rank = 0, world = 1;
-    int64_t slot_floats = 0;          // one layer's gathered output [B][Hq_total][D]
-    char* base = nullptr;             // [2 slots][slot_floats] floats, then flags[2][8], then done counter
+    int64_t slot_floats = 0;          // elements of one layer's gathered output [B][Hq_total][D]
+    char* base = nullptr;             // [2 slots][slot_floats] 64-bit words (epoch << 32 | float bits)
+    int64_t used[2] = {};             // words the last attention of each slot parity wrote (rows x heads x D)
+    uint32_t used_epoch[2] = {};      // and its epoch
     char* peer_base[8] = {};          // other ranks' bases, NULL for self
     bool peer_ipc[8] = {};            // opened from a CUDA IPC handle (closed on destroy)
     bool opened = false;
@@ -419,6 +419,7 @@ int launch_decode_mma(const AttnParams& p, const CUtensorMap& tk_sw, const CUten
 
 // Exchange fields of a decode launch that publishes its rows (exchange.cu).
 int exchange_params(const s1kv_exchange* ex, uint32_t epoch, int32_t head0, int32_t heads_total, AttnParams* ap);
+void exchange_record(s1kv_exchange* ex, uint32_t epoch, int64_t words);
 
 // Tensor-core prefix-hit prefill (prefill_tc.cu).
 bool prefill_tc_supported(int dtype, int D, int G, int block_size);

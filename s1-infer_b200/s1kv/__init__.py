@@ -654,19 +654,21 @@ def gather_heads(out_local, world, group=None, buf=None):
 
 
 class _DeviceArray:
-    """__cuda_array_interface__ view of device memory owned elsewhere."""
+    """__cuda_array_interface__ view of device memory owned elsewhere (fp32;
+    strides in bytes, None for contiguous)."""
 
-    def __init__(self, ptr, shape):
+    def __init__(self, ptr, shape, strides=None):
         self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4", "data": (ptr, False), "version": 3,
-                                         "strides": None}
+                                         "strides": strides}
 
 
 class PeerExchange:
     """Fused output exchange of a KV-head-sharded job (s1kv_exchange_*): the
-    decode kernels store each finished row into every rank's token-major
-    buffer [rows, heads_total, head_dim] over NVLink and signal the layer's
-    epoch; wait(epoch) makes the stream wait (bounded) for all ranks.  The
-    CUDA IPC handles are exchanged once through torch.distributed."""
+    decode kernels store each finished element, tagged with the layer's
+    epoch in one 64-bit word, into every rank's token-major buffer
+    [rows, heads_total, head_dim] over NVLink; wait(epoch) makes the stream
+    wait (bounded) until all ranks' words carry the epoch.  Epochs start at
+    1.  The CUDA IPC handles are exchanged once through torch.distributed."""
 
     def __init__(self, rank, world, rows, heads_total, head_dim, device=None, group=None, local=False):
         import torch
@@ -703,9 +705,9 @@ class PeerExchange:
                                                    epoch, _stream()))
 
     def wait(self, epoch, force=False):
-        """Makes the stream wait until every rank signalled `epoch`.  With one
-        rank the stream order already covers it, so nothing is launched
-        unless `force`."""
+        """Makes the stream wait until every rank's words of `epoch` arrived.
+        With one rank the stream order already covers it, so nothing is
+        launched unless `force`."""
         if self.world > 1 or force:
             check(self.L.s1kv_exchange_wait(self.h, epoch, _stream()))
 
@@ -719,13 +721,16 @@ class PeerExchange:
         return dst
 
     def output(self, epoch, rows=None):
-        """The gathered [rows, heads_total, head_dim] of `epoch` (a view of
-        the exchange's memory; valid until the slot is reused two epochs
-        later or the exchange is closed).  The two slots' tensors are made
-        once: a decode loop calls this every layer."""
+        """The gathered [rows, heads_total, head_dim] of `epoch` (a strided
+        fp32 view of the value halves of the exchange's words; valid until
+        the slot is reused two epochs later or the exchange is closed).  The
+        two slots' tensors are made once: a decode loop calls this every
+        layer."""
         import torch
         if not hasattr(self, "_slots"):
-            self._slots = [torch.as_tensor(_DeviceArray(self.L.s1kv_exchange_buffer(self.h, e), self.shape),
+            rows, heads, D = self.shape
+            strides = (heads * D * 8, D * 8, 8)
+            self._slots = [torch.as_tensor(_DeviceArray(self.L.s1kv_exchange_buffer(self.h, e), self.shape, strides),
                                            device="cuda") for e in (0, 1)]
         t = self._slots[epoch & 1]
         return t if rows is None else t[:rows]
