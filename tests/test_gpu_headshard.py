@@ -162,8 +162,8 @@ def test_two_gpu_fused_exchange_matches_oracle(tmp_path, oracle):
 
 
 @pytest.mark.gpu
-def test_exchange_wait_times_out_on_a_flag_nobody_sets(cuda):
-    """A one-rank exchange waiting for an epoch no kernel signals: the bounded
+def test_exchange_wait_times_out_on_an_epoch_nobody_wrote(cuda):
+    """A one-rank exchange waiting for an epoch no kernel wrote: the bounded
     wait gives up (about a second), the device error word reports the
     timeout, and the GPU keeps working."""
     import torch
