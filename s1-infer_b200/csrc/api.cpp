@@ -212,9 +212,13 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
         delete b;
         return st;
     }
-    // One upload of the step's metadata.
+    // One upload of the step's metadata.  The per-row records go up only
+    // with a decode batch's work list: query chunks take the tensor-core
+    // prefill (per-sequence records), and a chunk batch that falls back to
+    // the split-K kernels uploads its rows with its late-planned work list.
+    const int64_t up_rows = b->items_planned ? n_rows : 0;
     size_t o_slots = 0, o_pos = align16(o_slots + n_tok * 4), o_rows = align16(o_pos + n_tok * 4),
-           o_items = align16(o_rows + n_rows * sizeof(RowMeta)), o_pseq = align16(o_items + items.size() * sizeof(WorkItem)),
+           o_items = align16(o_rows + up_rows * sizeof(RowMeta)), o_pseq = align16(o_items + items.size() * sizeof(WorkItem)),
            o_qpos = align16(o_pseq + pseqs.size() * sizeof(PrefillSeq)),
            total = align16(o_qpos + (b->rows_are_tokens ? 0 : n_rows * 4));
     st = p->stager.acquire(total + 16, &b->seg);
@@ -225,7 +229,7 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
     char* h = b->seg->h;
     std::memcpy(h + o_slots, slots.data(), n_tok * 4);
     std::memcpy(h + o_pos, pos.data(), n_tok * 4);
-    std::memcpy(h + o_rows, b->rows.data(), n_rows * sizeof(RowMeta));
+    std::memcpy(h + o_rows, b->rows.data(), up_rows * sizeof(RowMeta));
     std::memcpy(h + o_items, items.data(), items.size() * sizeof(WorkItem));
     std::memcpy(h + o_pseq, pseqs.data(), pseqs.size() * sizeof(PrefillSeq));
     if (!b->rows_are_tokens) {
@@ -235,7 +239,7 @@ int s1kv_batch_begin(s1kv_pool* p, const uint64_t* seqs, const int32_t* n_append
     if (total) S1KV_CUDA(cudaMemcpyAsync(b->seg->d, h, total, cudaMemcpyHostToDevice, stream));
     b->d_slots = (const int32_t*)(b->seg->d + o_slots);
     b->d_pos = (const int32_t*)(b->seg->d + o_pos);
-    b->d_rows = (const RowMeta*)(b->seg->d + o_rows);
+    b->d_rows = up_rows ? (const RowMeta*)(b->seg->d + o_rows) : nullptr;
     b->d_items = (const WorkItem*)(b->seg->d + o_items);
     b->items_uploaded = b->items_planned;
     b->d_pseqs = (const PrefillSeq*)(b->seg->d + o_pseq);

@@ -241,8 +241,14 @@ struct StageSeg {
 
 struct Stager {
     static constexpr int kSegs = 6;
+    // Capacity every segment gets when the pool is created: growing one
+    // later allocates pinned memory and frees device memory (which
+    // synchronises the device) in the middle of a step.  1 MB holds the
+    // metadata of a step of about 100K appended tokens.
+    static constexpr size_t kInitialBytes = size_t(1) << 20;
     StageSeg seg[kSegs];
     int next = 0;
+    int reserve(size_t bytes);
     int acquire(size_t bytes, StageSeg** out);
     int release(StageSeg* s, cudaStream_t stream);
     void destroy();

@@ -92,6 +92,17 @@ int Stager::acquire(size_t bytes, StageSeg** out) {
     return S1KV_OK;
 }
 
+int Stager::reserve(size_t bytes) {
+    for (auto& s : seg) {
+        if (s.h || s.d) continue;  // a fresh stager's segments only (pool creation)
+        if (s.ev == nullptr) S1KV_CUDA(cudaEventCreateWithFlags(&s.ev, cudaEventDisableTiming));
+        S1KV_CUDA(cudaHostAlloc((void**)&s.h, bytes, cudaHostAllocDefault));
+        S1KV_CUDA(cudaMalloc((void**)&s.d, bytes));
+        s.cap = bytes;
+    }
+    return S1KV_OK;
+}
+
 int Stager::release(StageSeg* s, cudaStream_t stream) {
     s->in_use = false;
     S1KV_CUDA(cudaEventRecord(s->ev, stream));
@@ -461,6 +472,7 @@ int s1kv_pool_create(const s1kv_pool_desc* d, int device, s1kv_pool** out) {
             return set_error(S1KV_ENOMEM, "s1kv_pool_create: error word allocation failed");
         }
         int st = make_tensor_maps(p);
+        if (!st) st = p->stager.reserve(Stager::kInitialBytes);
         if (st) {
             s1kv_pool_destroy(p);
             return st;
