@@ -224,9 +224,10 @@ int s1kv_prefix_load_v1(s1kv_pool* pool, uint64_t seq, const char* path, int32_t
  * store is seen whole or not at all); s1kv_exchange_wait (device, bounded:
  * sets the timeout bit of the error word after about a second) makes the
  * stream wait until every word that the epoch's attention fills, on all
- * ranks, carries the epoch; it is a programmatic dependent launch, resident
- * while this rank's decode kernel finishes, and polls only after that
- * kernel completed.  Epochs start at 1 and increase by one per layer step;
+ * ranks, carries the epoch; it is a programmatic dependent launch that
+ * polls while this rank's decode kernel still finishes (the words carry
+ * their epoch), so dst of s1kv_exchange_wait_copy must not be read by the
+ * attention call of the same epoch.  Epochs start at 1 and increase by one per layer step;
  * every rank waits for each epoch (s1kv_exchange_wait or _wait_copy) on the
  * stream of its attention before its attention of the next epoch -- that
  * wait on all ranks' words is what makes reusing a slot two epochs later

@@ -32,9 +32,15 @@ size_t alloc_bytes(int64_t slot_floats) { return (size_t)2 * slot_floats * sizeo
 // set, the words of heads [head0, head0 + n_heads) go to dst [rows]
 // [n_heads][D] as floats.  A thread gives up after kWaitSpins polls in all
 // and sets the timeout bit (dst is then incomplete).  Launched as a
-// programmatic dependent launch: the CTAs may become resident while this
-// rank's decode kernel still runs and wait for it to complete
-// (griddepcontrol.wait), so the only waits left are on the other GPUs'.
+// programmatic dependent launch that does NOT wait for the decode kernel
+// before it (no griddepcontrol.wait): the words carry their epoch, so it
+// polls them while the decode kernel still merges splits and pushes rows,
+// and completes once every word has landed rather than when the decode
+// kernel's remote stores are acknowledged.  That is safe because the
+// decode kernel lets it launch only after its main loop (every kernel
+// before it in the stream has completed by then), this kernel writes only
+// dst, which the decode kernel never touches, and once every word is
+// present the decode kernel has done all its reads and counter resets.
 __device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
     uint64_t w;
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
@@ -43,7 +49,7 @@ __device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
 
 __global__ void exchange_wait_kernel(const uint64_t* slot, int64_t words, uint32_t epoch, int* err, int heads_total,
                                      int D, int head0, int n_heads, float* dst) {
-    pdl_enter();
+    pdl_trigger();
     uint32_t spins = 0;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < words; i0 += kWaitPer * stride) {
